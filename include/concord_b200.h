@@ -1,0 +1,203 @@
+/*
+ * concord_b200.h — C ABI of the B200-native Concord packed-word hot path.
+ *
+ * Every entry point takes plain device pointers, element counts / strides
+ * (in elements), and a `cudaStream_t` passed as `void*` (NULL = legacy
+ * default stream).  Nothing here allocates device memory: scratch space is
+ * passed in by the caller and its size is reported by the matching
+ * `*_workspace_bytes` query.  Every entry point returns 0 on success or a
+ * negative `CONCORD_E*` code; `concord_last_error()` gives a one-line
+ * message for the calling thread.  bf16 tensors are passed as `uint16_t*`
+ * (the raw bf16 bit patterns).
+ *
+ * Packed word layout (one int32 per parameter):
+ *   bits 31:16  s_fast  int16   fast accumulator, mantissa units
+ *   bits 15:8   s_slow  int8    slow position, x128 mantissa units
+ *   bits  7:0   v_slow  int8    anchor,        x128 mantissa units
+ *   weight = (128*s_slow + s_fast + 128*v_slow) * 2^(row_exp + col_exp - 15)
+ *
+ * Reference interfaces replaced (Theophite/Concord, concord/packed_b.py):
+ *   concord_step          <- apply_packed_adamw / _apply_packed_adamw_kernel
+ *                            (packed_b.py:863-951, 422-703) and
+ *                            apply_packed_sgd / _apply_packed_sgd_kernel
+ *                            (packed_b.py:362-394, 173-312)
+ *   concord_vhat_update   <- the Adafactor v_row/v_col EMA + 1/sum(v_row)
+ *                            in FusedConcordLinearPackedB.backward
+ *                            (packed_b.py:1278-1303), plus the row/col max
+ *                            zeroing (1281-1283) and the step-counter bump
+ *                            (910-911)
+ *   concord_salt_bump     <- _get_step_counter(...).add_(1) (packed_b.py:376-377, 910-911)
+ *   concord_rebalance     <- rebalance_packed / _rebalance_packed_decide_kernel
+ *                            (packed_b.py:1129-1190, 959-1095) and the
+ *                            high-watermark fold + seed bump of
+ *                            ConcordLinearPackedB.rebalance (1792-1814)
+ *   concord_materialize   <- materialize_packed_bf16 (packed_b.py:120-170),
+ *                            consolidated_weight (1632-1649)
+ *   concord_quantize      <- ConcordLinearPackedB.load_weights (1570-1603),
+ *                            load_weights_finetune (1816-1856)
+ *   concord_coherence     <- measure_coherence / gate_coherence_from_fields
+ *                            (packed_b.py:2081-2106)
+ */
+#ifndef CONCORD_B200_H
+#define CONCORD_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CONCORD_ABI_VERSION 1
+
+/* status codes */
+#define CONCORD_OK            0
+#define CONCORD_EINVAL       -1  /* bad argument: null pointer, negative size */
+#define CONCORD_ESHAPE       -2  /* shape / stride not supported              */
+#define CONCORD_EALIGN       -3  /* pointer alignment not supported           */
+#define CONCORD_EWORKSPACE   -4  /* workspace missing or too small            */
+#define CONCORD_ELAUNCH      -5  /* CUDA launch / runtime error               */
+#define CONCORD_ENODEVICE    -6  /* no usable CUDA device                      */
+#define CONCORD_ETOOBIG      -7  /* size above a fixed maximum                */
+
+/* step-kernel flag bits (the reference's Triton constexprs, packed_b.py:451-458) */
+#define CONCORD_F_MASS_PRESERVE   (1u << 0)
+#define CONCORD_F_APPLY_CHASE     (1u << 1)
+#define CONCORD_F_TRACK_REBALANCE (1u << 2)
+#define CONCORD_F_GF_TRUST        (1u << 3)
+#define CONCORD_F_GF_CONSOL       (1u << 4)
+#define CONCORD_F_COHPRE          (1u << 5)
+#define CONCORD_F_FIXED_COH       (1u << 6)
+#define CONCORD_F_RATIO_COH       (1u << 7)
+
+#define CONCORD_KIND_ADAMW 0
+#define CONCORD_KIND_SGD   1
+
+/*
+ * Launch-time scalars of one packed step.  Every float is the fp32 value
+ * the kernel multiplies with.  Where the reference combines two host
+ * scalars before they meet a tensor (e.g. `1.0 - alpha_v_fast`), the
+ * combined value is computed on the host in double and rounded once to
+ * fp32 — the `one_minus_*` and `alpha_gate_gain` fields carry those.
+ */
+typedef struct concord_step_params {
+    int32_t  kind;                  /* CONCORD_KIND_ADAMW / CONCORD_KIND_SGD */
+    int32_t  mantissa_bias;         /* 15 */
+    uint32_t flags;                 /* CONCORD_F_* */
+    float alpha;                    /* chase rate */
+    float beta1;
+    float weight_decay;
+    float step_cap;
+    float v_scale;
+    float precond_p;
+    float gf_consol;                /* evaporation kappa */
+    float drift_cancel_C;
+    float alpha_v_fast;
+    float one_minus_alpha_v_fast;   /* fp32(1.0 - alpha_v_fast), double-folded */
+    float wd_sv;
+    float wd_sf;
+    float gf_trust_delta_sq;
+    float gate_gain;
+    float chase_floor;
+    float one_minus_chase_floor;    /* fp32(1.0 - chase_floor) */
+    float leak_floor;
+    float one_minus_leak_floor;     /* fp32(1.0 - leak_floor) */
+    float alpha_gate_gain;          /* fp32(alpha * 1.0 * gate_gain): chase gain when no gate tensor */
+} concord_step_params;
+
+int         concord_abi_version(void);
+const char* concord_last_error(void);
+
+/* *salt += 1 on the stream (the reference's per-device step counter). */
+int concord_salt_bump(int32_t* salt, void* stream);
+
+/*
+ * Adafactor second-moment update from a bf16 gradient [N,K] (row stride ldg):
+ *   v_row = b2*v_row + (1-b2)*sum_k g^2,  v_col likewise over n,
+ *   sum_v_inv = 1 / max(sum_n v_row, 1e-30).
+ * Sums run in a fixed order (deterministic).  Also zeroes row_max[N] and
+ * col_max[K] when they are non-NULL, and bumps *salt when it is non-NULL,
+ * so that a following concord_step sees the reference's pre-launch state.
+ * `workspace` must hold concord_vhat_workspace_bytes(N, K) bytes and be
+ * zero-filled before its first use (the kernel leaves it reusable).
+ */
+size_t concord_vhat_workspace_bytes(int64_t N, int64_t K);
+int concord_vhat_update(const uint16_t* grad, int64_t ldg, int64_t N, int64_t K,
+                        float* v_row, float* v_col, float* sum_v_inv,
+                        float beta2, float one_minus_beta2,
+                        int32_t* row_max, int32_t* col_max, int32_t* salt,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * One packed optimizer step over rows [0,N) of a (row-)shard whose first
+ * row is global row `row0` (0 when unsharded).  Mutates packed (and
+ * coh_pre when CONCORD_F_COHPRE) in place, writes the new bf16 weight to
+ * wbuf, and atomic-maxes |m_eff| into row_max[N]/col_max[K] when
+ * CONCORD_F_TRACK_REBALANCE.  v_row/v_col/sum_v_inv are read only when a
+ * flag needs them.  lr, eps and salt are device scalars.  coh_stats, when
+ * non-NULL, receives (sum of coh, element count) as two doubles added
+ * atomically (the fused coherence meter); it is only written when the
+ * flags compute coh.
+ */
+int concord_step(const concord_step_params* p,
+                 int32_t* packed, int64_t ldp,
+                 const uint16_t* grad, int64_t ldg,
+                 uint16_t* wbuf, int64_t ldw,
+                 const int8_t* row_exp, const int8_t* col_exp,
+                 int32_t* row_max, int32_t* col_max,
+                 const float* v_row, const float* v_col, const float* sum_v_inv,
+                 float* coh_pre, int64_t ldc,
+                 const float* lr, const float* eps, const int32_t* salt,
+                 int64_t N, int64_t K, int64_t row0,
+                 double* coh_stats, void* stream);
+
+/*
+ * Rebalance ratchet.  Folds row_max/col_max into the high-watermarks (when
+ * non-NULL), bumps *seed, decides per-row/col exponent ticks from the
+ * PRE-launch exponents, SR-right-shifts the three fields where a tick-up
+ * fires (Philox4x32-10 uniforms keyed by (seed, n*K+k + {0,NK,2NK})), and
+ * left-shifts where a tick-down fires (allow_tickdown only).  N_total is
+ * the global row count and row0 the first global row (Philox offsets use
+ * global indices).  fired_out (nullable, device int32) is set to 1 when any
+ * exponent moved, else 0.  Workspace: concord_rebalance_workspace_bytes(N, K),
+ * zero-filled before first use.
+ */
+size_t concord_rebalance_workspace_bytes(int64_t N, int64_t K);
+int concord_rebalance(int32_t* packed, int64_t ldp,
+                      int8_t* row_exp, int8_t* col_exp,
+                      const int32_t* row_max, const int32_t* col_max,
+                      int32_t* row_hwm, int32_t* col_hwm,
+                      int32_t* seed, int32_t max_m, int32_t exp_max, int32_t exp_min,
+                      int32_t allow_tickdown,
+                      int64_t N, int64_t K, int64_t row0, int64_t N_total,
+                      int32_t* fired_out,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* bf16 weight = (m_eff or the slow part only) * 2^(row_exp+col_exp-bias), RNE. */
+int concord_materialize(const int32_t* packed, int64_t ldp,
+                        const int8_t* row_exp, const int8_t* col_exp,
+                        uint16_t* out, int64_t ldo, int64_t N, int64_t K,
+                        int32_t mantissa_bias, int32_t consolidated, void* stream);
+
+/*
+ * fp32 W [N,K] -> packed words + row_exp (col_exp zeroed).  finetune=0:
+ * whole mantissa in s_fast (load_weights); finetune=1: split half to
+ * v_slow, rest to s_slow, residual to s_fast (load_weights_finetune).
+ */
+int concord_quantize(const float* W, int64_t ldw, int32_t* packed, int64_t ldp,
+                     int8_t* row_exp, int8_t* col_exp, int64_t N, int64_t K,
+                     int32_t mantissa_bias, int32_t exp_min, int32_t exp_max,
+                     int32_t finetune, void* stream);
+
+/*
+ * Wiener coherence of the packed state (measure_coherence):
+ * out[0] += sum of coh (double), out[1] += element count.  The caller
+ * zeroes out[] first.
+ */
+int concord_coherence(const int32_t* packed, int64_t ldp, int64_t N, int64_t K,
+                      float drift_cancel_C, double* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CONCORD_B200_H */
