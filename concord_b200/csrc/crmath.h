@@ -1,0 +1,237 @@
+// crmath.h — correctly rounded fp32 log2 / exp2 for the packed step.
+//
+// The reference computes the Adam denominator as exp2(p * log2(v + eps))
+// (concord/packed_b.py:557) and the shared-exponent scales as exp2(+-e)
+// (packed_b.py:491-492).  Parity with the reference's outputs is pinned to
+// correctly rounded exp2/log2, so both functions here return the fp32 value
+// nearest to the exact result, with the same bits on the host and the GPU:
+//   fast path:  double-precision evaluation (relative error < 2^-49) plus a
+//               rounding test (Ziv): if x + err and x - err round to the same
+//               float, that float is the correctly rounded result;
+//   slow path:  (about 1 call in 2^22) double-double evaluation with error
+//               below 2^-100, rounded to fp32 through round-to-odd.
+// Only IEEE double add/mul/div and explicit fma are used; compile host code
+// with -ffp-contract=off and device code with -fmad=false so that nothing
+// is contracted behind the code's back.
+#pragma once
+
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+
+#if defined(__CUDACC__)
+#define CR_HD __host__ __device__ __forceinline__
+#else
+#define CR_HD static inline
+#endif
+
+namespace crmath {
+
+CR_HD double u2d(uint64_t u) {
+#if defined(__CUDA_ARCH__)
+    return __longlong_as_double((long long)u);
+#else
+    double d; memcpy(&d, &u, 8); return d;
+#endif
+}
+CR_HD uint64_t d2u(double d) {
+#if defined(__CUDA_ARCH__)
+    return (uint64_t)__double_as_longlong(d);
+#else
+    uint64_t u; memcpy(&u, &d, 8); return u;
+#endif
+}
+CR_HD uint32_t f2u(float f) {
+#if defined(__CUDA_ARCH__)
+    return __float_as_uint(f);
+#else
+    uint32_t u; memcpy(&u, &f, 4); return u;
+#endif
+}
+CR_HD float u2f(uint32_t u) {
+#if defined(__CUDA_ARCH__)
+    return __uint_as_float(u);
+#else
+    float f; memcpy(&f, &u, 4); return f;
+#endif
+}
+
+// 2^n as a double, n in [-1022, 1023]
+CR_HD double pow2d(int n) { return u2d((uint64_t)(int64_t)(n + 1023) << 52); }
+
+// ---- double-double arithmetic (value = hi + lo, |lo| <= ulp(hi)/2) ----
+struct dd { double hi, lo; };
+
+CR_HD dd quick_two_sum(double a, double b) { double s = a + b; return {s, b - (s - a)}; }
+CR_HD dd two_sum(double a, double b) {
+    double s = a + b, bb = s - a;
+    return {s, (a - (s - bb)) + (b - bb)};
+}
+CR_HD dd two_prod(double a, double b) { double p = a * b; return {p, fma(a, b, -p)}; }
+CR_HD dd dd_add(dd a, dd b) {
+    dd s = two_sum(a.hi, b.hi), t = two_sum(a.lo, b.lo);
+    s.lo += t.hi;
+    s = quick_two_sum(s.hi, s.lo);
+    s.lo += t.lo;
+    return quick_two_sum(s.hi, s.lo);
+}
+CR_HD dd dd_mul(dd a, dd b) {
+    dd p = two_prod(a.hi, b.hi);
+    p.lo += a.hi * b.lo + a.lo * b.hi;
+    return quick_two_sum(p.hi, p.lo);
+}
+CR_HD dd dd_mul_d(dd a, double b) {
+    dd p = two_prod(a.hi, b);
+    p.lo += a.lo * b;
+    return quick_two_sum(p.hi, p.lo);
+}
+CR_HD dd dd_div_d(dd a, double b) {  // a / b, b a double
+    double q1 = a.hi / b;
+    dd r = dd_add(a, dd{-q1 * b, -fma(q1, b, -q1 * b)});
+    double q2 = r.hi / b;
+    r = dd_add(r, dd{-q2 * b, -fma(q2, b, -q2 * b)});
+    double q3 = r.hi / b;
+    dd q = quick_two_sum(q1, q2);
+    return dd_add(q, dd{q3, 0.0});
+}
+CR_HD dd dd_div(dd a, dd b) {
+    double q1 = a.hi / b.hi;
+    dd r = dd_add(a, dd_mul_d(b, -q1));
+    double q2 = r.hi / b.hi;
+    r = dd_add(r, dd_mul_d(b, -q2));
+    double q3 = r.hi / b.hi;
+    dd q = quick_two_sum(q1, q2);
+    return dd_add(q, dd{q3, 0.0});
+}
+
+// Round hi+lo to fp32 (nearest-even) via round-to-odd at 53 bits.
+CR_HD float dd_to_float(dd v) {
+    if (v.lo == 0.0 || v.hi != v.hi) return (float)v.hi;
+    uint64_t u = d2u(v.hi);
+    if ((v.lo > 0.0) != (v.hi > 0.0)) u -= 1;  // truncate toward zero
+    u |= 1;                                     // sticky bit
+    return (float)u2d(u);
+}
+
+// ---- constants ----
+// 1/ln2 and ln2 as double-double (hi = nearest double, lo = remainder)
+#define CR_INVLN2_HI 1.4426950408889634
+#define CR_INVLN2_LO 2.0355273740931033e-17
+#define CR_LN2_HI 0.6931471805599453
+#define CR_LN2_LO 2.3190468138462996e-17
+
+// Decompose finite x > 0 as m * 2^e with m in [sqrt(1/2), sqrt(2)).
+CR_HD void log_reduce(float x, float* m_out, int* e_out) {
+    uint32_t b = f2u(x);
+    int e = 0;
+    if (b < 0x00800000u) {  // subnormal: scale by 2^24 (exact)
+        x = x * 16777216.0f;
+        b = f2u(x);
+        e = -24;
+    }
+    e += (int)((b >> 23) & 0xffu) - 127;
+    float m = u2f((b & 0x007fffffu) | 0x3f800000u);
+    if (m > 1.41421353816986083984375f) { m = m * 0.5f; e += 1; }
+    *m_out = m;
+    *e_out = e;
+}
+
+// log(m) = 2 s (1 + z/3 + z^2/5 + ...), s = (m-1)/(m+1), z = s^2, |z| < 0.0295
+CR_HD float log2f_slow(float m, int e) {
+    double md = (double)m;
+    double num = md - 1.0, den = md + 1.0;  // exact
+    double sh = num / den;
+    dd s = quick_two_sum(sh, fma(-sh, den, num) / den);
+    dd z = dd_mul(s, s);
+    dd p = dd{1.0 / 43.0, fma(-(1.0 / 43.0), 43.0, 1.0) / 43.0};
+    for (int k = 20; k >= 0; --k) {
+        double c = (double)(2 * k + 1);
+        double ch = 1.0 / c;
+        p = dd_add(dd_mul(p, z), dd{ch, fma(-ch, c, 1.0) / c});
+    }
+    dd lnm = dd_mul(s, p);
+    lnm.hi *= 2.0; lnm.lo *= 2.0;
+    dd l2 = dd_mul(lnm, dd{CR_INVLN2_HI, CR_INVLN2_LO});
+    dd L = dd_add(dd{(double)e, 0.0}, l2);
+    return dd_to_float(L);
+}
+
+template <bool FORCE_SLOW = false>
+CR_HD float cr_log2f(float x) {
+    if (!(x > 0.0f)) {
+        if (x == 0.0f) return -INFINITY;
+        return NAN;  // negative or NaN
+    }
+    if (x == INFINITY) return INFINITY;
+    float m; int e;
+    log_reduce(x, &m, &e);
+    double md = (double)m;
+    double s = (md - 1.0) / (md + 1.0);
+    double z = s * s;
+    double p = 1.0 / 21.0;
+    p = fma(p, z, 1.0 / 19.0);
+    p = fma(p, z, 1.0 / 17.0);
+    p = fma(p, z, 1.0 / 15.0);
+    p = fma(p, z, 1.0 / 13.0);
+    p = fma(p, z, 1.0 / 11.0);
+    p = fma(p, z, 1.0 / 9.0);
+    p = fma(p, z, 1.0 / 7.0);
+    p = fma(p, z, 1.0 / 5.0);
+    p = fma(p, z, 1.0 / 3.0);
+    p = fma(p, z, 1.0);
+    double l2 = (2.0 * s) * p * CR_INVLN2_HI;
+    double L = (double)e + l2;
+    double err = fabs(L) * 0x1p-46;
+    float a = (float)(L + err), b = (float)(L - err);
+    if (!FORCE_SLOW && a == b) return a;
+    return log2f_slow(m, e);
+}
+
+// 2^f for |f| <= 1/2 in double-double: exp(t), t = f ln2, Taylor to t^24/24!
+CR_HD dd exp2_frac_dd(double f) {
+    dd t = dd_mul_d(dd{CR_LN2_HI, CR_LN2_LO}, f);
+    dd sum = dd{1.0, 0.0}, term = dd{1.0, 0.0};
+    for (int k = 1; k <= 24; ++k) {
+        term = dd_div_d(dd_mul(term, t), (double)k);
+        sum = dd_add(sum, term);
+    }
+    return sum;
+}
+
+template <bool FORCE_SLOW = false>
+CR_HD float cr_exp2f(float y) {
+    if (y != y) return y;
+    if (y >= 128.0f) return INFINITY;
+    if (y < -150.0f) return 0.0f;
+    double yd = (double)y;
+    double n = rint(yd);
+    double f = yd - n;  // exact, |f| <= 1/2
+    int ni = (int)n;
+    if (f == 0.0) return (float)pow2d(ni);  // exact power of two (subnormals included)
+    double t = f * CR_LN2_HI;
+    double p = 1.0 / 87178291200.0;               // 1/14!
+    p = fma(p, t, 1.0 / 6227020800.0);            // 1/13!
+    p = fma(p, t, 1.0 / 479001600.0);             // 1/12!
+    p = fma(p, t, 1.0 / 39916800.0);
+    p = fma(p, t, 1.0 / 3628800.0);
+    p = fma(p, t, 1.0 / 362880.0);
+    p = fma(p, t, 1.0 / 40320.0);
+    p = fma(p, t, 1.0 / 5040.0);
+    p = fma(p, t, 1.0 / 720.0);
+    p = fma(p, t, 1.0 / 120.0);
+    p = fma(p, t, 1.0 / 24.0);
+    p = fma(p, t, 1.0 / 6.0);
+    p = fma(p, t, 0.5);
+    p = fma(p, t, 1.0);
+    p = fma(p, t, 1.0);
+    double sc = pow2d(ni);
+    double r = p * sc;
+    double err = r * 0x1p-46;
+    float a = (float)(r + err), b = (float)(r - err);
+    if (!FORCE_SLOW && a == b) return a;
+    dd v = exp2_frac_dd(f);
+    v.hi *= sc; v.lo *= sc;  // exact scaling by a power of two
+    return dd_to_float(v);
+}
+
+}  // namespace crmath

@@ -1,0 +1,205 @@
+// vhat.cu — Adafactor rank-1 second-moment update for the packed step.
+//
+// Replaces the torch ops in FusedConcordLinearPackedB.backward
+// (concord/packed_b.py:1288-1303):
+//   v_row = b2*v_row + (1-b2)*sum_k g^2;  v_col = b2*v_col + (1-b2)*sum_n g^2;
+//   sum_v_inv = 1 / max(sum_n v_row, 1e-30)
+// in one launch that reads the bf16 gradient once.  Grid: (column slabs of
+// 256, row blocks of 128); each block writes a row partial per (row, slab)
+// and a column partial per (column, row block) into the workspace.  The last
+// block to finish a slab folds that slab's column partials into v_col; the
+// last block to finish a row block folds its row partials into v_row; the
+// last row block overall computes sum_v_inv.  "Last" is decided by atomic
+// arrival counters, so nothing spins.  Every sum runs in a fixed order
+// (spelled out in oracle/concord_oracle.c:oracle_vhat), so the result is
+// deterministic and bit-identical to the CPU restatement.
+//
+// The launch also zeroes row_max/col_max and bumps the step salt, which the
+// reference does with separate launches before its apply kernel
+// (packed_b.py:1281-1283, 910-911).
+#include "common.cuh"
+
+namespace concord {
+
+constexpr int VH_THREADS = 256;
+constexpr int VH_COLS = 256;
+constexpr int VH_ROWS = 128;
+
+struct VhatArgs {
+    const uint16_t* grad; int64_t ldg;
+    int64_t N, K;
+    float* v_row; float* v_col; float* sum_v_inv;
+    float b2, omb2;
+    int32_t* row_max; int32_t* col_max; int32_t* salt;
+    float* rp;        // [ncs][N] row partials
+    float* cp;        // [nrb][K] column partials
+    unsigned* cnt;    // [nrb] row-block arrivals, [ncs] slab arrivals, [1] global
+    int ncs, nrb;
+    bool vec;
+};
+
+__global__ void __launch_bounds__(VH_THREADS) vhat_kernel(VhatArgs A) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int cs = blockIdx.x, rb = blockIdx.y;
+    const int64_t k0 = (int64_t)cs * VH_COLS + lane * 8;
+    __shared__ float colsm[VH_THREADS / 32][VH_COLS];
+    __shared__ float red[VH_THREADS];
+    __shared__ int flags[2];
+
+    if (A.salt && cs == 0 && rb == 0 && threadIdx.x == 0) *A.salt += 1;
+    if (A.row_max && cs == 0 && threadIdx.x < VH_ROWS) {
+        int64_t n = (int64_t)rb * VH_ROWS + threadIdx.x;
+        if (n < A.N) A.row_max[n] = 0;
+    }
+    if (A.col_max && rb == 0) {
+        int64_t k = (int64_t)cs * VH_COLS + threadIdx.x;
+        if (k < A.K) A.col_max[k] = 0;
+    }
+
+    float cacc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) cacc[j] = 0.0f;
+    for (int i = 0; i < VH_ROWS / 8; ++i) {
+        const int64_t n = (int64_t)rb * VH_ROWS + warp + 8 * i;
+        float g2[8];
+        if (n < A.N) {
+            const uint16_t* gp = A.grad + n * A.ldg + k0;
+            if (A.vec && k0 < A.K) {
+                uint4 v = __ldg(reinterpret_cast<const uint4*>(gp));
+                uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    float g = bf16_to_f32((w[j >> 1] >> ((j & 1) * 16)) & 0xffffu);
+                    g2[j] = g * g;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    float g = (k0 + j < A.K) ? bf16_to_f32(gp[j]) : 0.0f;
+                    g2[j] = g * g;
+                }
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) g2[j] = 0.0f;
+        }
+        // row partial: lane sum of 8 columns, then xor butterfly
+        float s = g2[0];
+#pragma unroll
+        for (int j = 1; j < 8; ++j) s = s + g2[j];
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) s = s + __shfl_xor_sync(0xffffffffu, s, o);
+        if (lane == 0 && n < A.N) A.rp[(int64_t)cs * A.N + n] = s;
+        // column partial: this warp's rows in order
+#pragma unroll
+        for (int j = 0; j < 8; ++j) cacc[j] = (i == 0) ? g2[j] : cacc[j] + g2[j];
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) colsm[warp][lane * 8 + j] = cacc[j];
+    __syncthreads();
+    {
+        float tot = colsm[0][threadIdx.x];
+#pragma unroll
+        for (int w = 1; w < VH_THREADS / 32; ++w) tot = tot + colsm[w][threadIdx.x];
+        const int64_t col = (int64_t)cs * VH_COLS + threadIdx.x;
+        if (col < A.K) A.cp[(int64_t)rb * A.K + col] = tot;
+    }
+    __threadfence();
+    __syncthreads();
+    unsigned* cnt_rb = A.cnt;
+    unsigned* cnt_cs = A.cnt + A.nrb;
+    unsigned* cnt_g = A.cnt + A.nrb + A.ncs;
+    if (threadIdx.x == 0) {
+        flags[0] = atomicAdd(cnt_cs + cs, 1u) == (unsigned)(A.nrb - 1);
+        flags[1] = atomicAdd(cnt_rb + rb, 1u) == (unsigned)(A.ncs - 1);
+    }
+    __syncthreads();
+    if (flags[0]) {  // last block of this column slab: finish v_col
+        __threadfence();
+        const int64_t col = (int64_t)cs * VH_COLS + threadIdx.x;
+        if (col < A.K) {
+            float t = __ldcg(A.cp + col);
+            for (int b = 1; b < A.nrb; ++b) t = t + __ldcg(A.cp + (int64_t)b * A.K + col);
+            A.v_col[col] = A.b2 * A.v_col[col] + A.omb2 * t;
+        }
+        if (threadIdx.x == 0) cnt_cs[cs] = 0;
+    }
+    if (flags[1]) {  // last block of this row block: finish v_row, maybe sum_v
+        __threadfence();
+        if (threadIdx.x < VH_ROWS) {
+            const int64_t n = (int64_t)rb * VH_ROWS + threadIdx.x;
+            if (n < A.N) {
+                float t = __ldcg(A.rp + n);
+                for (int c = 1; c < A.ncs; ++c) t = t + __ldcg(A.rp + (int64_t)c * A.N + n);
+                A.v_row[n] = A.b2 * A.v_row[n] + A.omb2 * t;
+            }
+        }
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            cnt_rb[rb] = 0;
+            flags[0] = atomicAdd(cnt_g, 1u) == (unsigned)(A.nrb - 1);
+        }
+        __syncthreads();
+        if (flags[0]) {
+            __threadfence();
+            float acc = 0.0f;
+            for (int64_t n = threadIdx.x; n < A.N; n += VH_THREADS) acc = acc + __ldcg(A.v_row + n);
+            red[threadIdx.x] = acc;
+            __syncthreads();
+            for (int s = VH_THREADS / 2; s >= 1; s >>= 1) {
+                if (threadIdx.x < s) red[threadIdx.x] = red[threadIdx.x] + red[threadIdx.x + s];
+                __syncthreads();
+            }
+            if (threadIdx.x == 0) {
+                float sv = np_max(red[0], 1e-30f);
+                *A.sum_v_inv = 1.0f / sv;
+                *cnt_g = 0;
+            }
+        }
+    }
+}
+
+}  // namespace concord
+
+using namespace concord;
+
+static void vhat_layout(int64_t N, int64_t K, int* ncs, int* nrb, size_t* off_rp, size_t* off_cp,
+                        size_t* total) {
+    *ncs = (int)((K + VH_COLS - 1) / VH_COLS);
+    *nrb = (int)((N + VH_ROWS - 1) / VH_ROWS);
+    size_t cnt_bytes = ((size_t)(*nrb + *ncs + 1) * sizeof(unsigned) + 255) / 256 * 256;
+    *off_rp = cnt_bytes;
+    size_t rp_bytes = ((size_t)(*ncs) * (size_t)N * sizeof(float) + 255) / 256 * 256;
+    *off_cp = cnt_bytes + rp_bytes;
+    *total = *off_cp + (size_t)(*nrb) * (size_t)K * sizeof(float);
+}
+
+extern "C" size_t concord_vhat_workspace_bytes(int64_t N, int64_t K) {
+    if (N <= 0 || K <= 0) return 0;
+    int ncs, nrb; size_t a, b, t;
+    vhat_layout(N, K, &ncs, &nrb, &a, &b, &t);
+    return t;
+}
+
+extern "C" int concord_vhat_update(const uint16_t* grad, int64_t ldg, int64_t N, int64_t K,
+                                   float* v_row, float* v_col, float* sum_v_inv, float beta2,
+                                   float one_minus_beta2, int32_t* row_max, int32_t* col_max,
+                                   int32_t* salt, void* workspace, size_t workspace_bytes,
+                                   void* stream) {
+    if (!grad || !v_row || !v_col || !sum_v_inv) return fail(CONCORD_EINVAL, "concord_vhat_update: null pointer");
+    if (N <= 0 || K <= 0 || ldg < K) return fail(CONCORD_ESHAPE, "concord_vhat_update: bad shape/stride");
+    int ncs, nrb; size_t off_rp, off_cp, total;
+    vhat_layout(N, K, &ncs, &nrb, &off_rp, &off_cp, &total);
+    if (!workspace || workspace_bytes < total)
+        return fail(CONCORD_EWORKSPACE, "concord_vhat_update: workspace smaller than concord_vhat_workspace_bytes(N, K)");
+    if (nrb > 65535) return fail(CONCORD_ETOOBIG, "concord_vhat_update: too many rows for one launch");
+    char* ws = static_cast<char*>(workspace);
+    VhatArgs A{grad, ldg, N, K, v_row, v_col, sum_v_inv, beta2, one_minus_beta2, row_max, col_max, salt,
+               reinterpret_cast<float*>(ws + off_rp), reinterpret_cast<float*>(ws + off_cp),
+               reinterpret_cast<unsigned*>(ws), ncs, nrb,
+               (K % 8 == 0) && (ldg % 8 == 0) && aligned(grad, 16)};
+    dim3 grid((unsigned)ncs, (unsigned)nrb);
+    vhat_kernel<<<grid, VH_THREADS, 0, as_stream(stream)>>>(A);
+    return check_launch("concord_vhat_update");
+}
