@@ -11,6 +11,7 @@ library is missing or a tensor is not on a CUDA device.  The dense GEMMs of
 forward / dX / dW run through `concord_b200.gemm`.
 """
 import ctypes
+from types import SimpleNamespace
 
 import torch
 import torch.nn as nn
@@ -370,11 +371,12 @@ def _accumulate_reb_stats(packed_w, row_exp, col_exp, row_max, col_max, MAX_M, E
 # Autograd Function + nn.Module (packed_b.py:1197-1856)
 # ============================================================
 
-def _packed_backward_step(ctx, grad_W):
+def _packed_backward_step(ctx, grad_W, step_events=None):
     """The optimizer half of the backward (packed_b.py:1278-1337).
 
     One launch updates v_row/v_col/sum_v_inv (and zeroes the row/col max
     buffers, bumps the salt); one launch runs the fused packed step.
+    `step_events` (optional [_, start, end] CUDA events) bracket the step launch.
     """
     track = bool(ctx.track_rebalance)
     rmax = ctx.row_max_buf if track else None
@@ -390,6 +392,8 @@ def _packed_backward_step(ctx, grad_W):
             rmax.zero_()
             cmax.zero_()
         _salt_bump(salt)
+    if step_events is not None:
+        step_events[1].record()
     if ctx.optimizer_kind == 'adamw':
         apply_packed_adamw(
             ctx.packed_w, grad_W, ctx.weight_buf, ctx.row_exp, ctx.col_exp,
@@ -409,6 +413,8 @@ def _packed_backward_step(ctx, grad_W):
             alpha=ctx.alpha, beta1=ctx.beta1, alpha_v_fast=ctx.alpha_v_fast,
             mass_preserve=ctx.mass_preserve, track_rebalance=ctx.track_rebalance,
             bump_salt=False)
+    if step_events is not None:
+        step_events[2].record()
 
 
 _CTX_FIELDS = ("packed_w", "row_exp", "col_exp", "lr", "alpha", "beta1", "mantissa_bias",
@@ -709,6 +715,16 @@ class ConcordLinearPackedB(nn.Module):
         y = FusedConcordLinearPackedB.apply(x, self.packed_w, self.row_exp, self.col_exp,
                                             self.bias, *self._apply_args(wbuf, rmbuf, cmbuf))
         return y.to(in_dtype)
+
+    @torch.no_grad()
+    def optimizer_step(self, grad_W, coh_stats=None, step_events=None):
+        """Run the optimizer half of the backward for a given bf16 dW [N, K]
+        (what the autograd backward does after its GEMMs)."""
+        wbuf, rmbuf, cmbuf = self._ensure_buffers()
+        vals = (self.packed_w, self.row_exp, self.col_exp) + self._apply_args(wbuf, rmbuf, cmbuf)[:-1]
+        ctx = SimpleNamespace(**dict(zip(_CTX_FIELDS, vals)))
+        ctx.coh_stats = coh_stats if coh_stats is not None else self.coh_stats
+        _packed_backward_step(ctx, grad_W.contiguous(), step_events)
 
     @torch.no_grad()
     def rebalance(self, fired_out=None):
