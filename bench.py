@@ -258,8 +258,8 @@ def base_line(args, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--rows", type=int, default=N)
     ap.add_argument("--cols", type=int, default=K)
@@ -275,9 +275,12 @@ def main():
             return
         # the reference path is Python+Triton with no CPU build; its CPU
         # implementation is the oracle port, run on every host core
-        rows = 4096
+        # size each step's sample so the whole run stays near one minute
+        _, t64 = cpu_baseline(rows=max(64, cores), threads=cores)
+        per_row = t64 / max(64, cores)
+        rows = int(min(4096, max(cores, 60.0 / max(1, args.steps + args.warmup) / per_row)))
         for _ in range(args.warmup):
-            cpu_baseline(rows=256, threads=cores)
+            cpu_baseline(rows=rows, threads=cores)
         vals = [cpu_baseline(rows=rows, threads=cores)[0] for _ in range(args.steps)]
         v = statistics.mean(vals)
         d = base_line(args, 1)

@@ -124,3 +124,38 @@ def f32_to_bf16(x):
 
 def bf16_to_f32(h):
     return (np.asarray(h, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def step_threaded(params, packed, grad_bf16, wbuf, row_exp, col_exp, row_max, col_max,
+                  v_row, v_col, sum_v_inv, coh_pre, lr, eps, salt, threads=8, row0=0):
+    """oracle_step split over row blocks on host threads (ctypes drops the GIL).
+
+    Row/col maxima are merged after the threads finish, so the result equals
+    the single-threaded call."""
+    import threading
+    N, K = packed.shape
+    bounds = np.linspace(0, N, threads + 1).astype(int)
+    cms = []
+    ths = []
+    for a, b in zip(bounds[:-1], bounds[1:]):
+        if b <= a:
+            continue
+        cm = np.zeros(K, np.int32)
+        cms.append(cm)
+        p, g, w = packed[a:b], grad_bf16[a:b], wbuf[a:b]
+        cp = coh_pre[a:b] if coh_pre is not None else None
+
+        def work(p=p, g=g, w=w, cp=cp, a=a, b=b, cm=cm):
+            rm = row_max[a:b] if row_max is not None else None
+            lib().oracle_step(
+                ctypes.byref(params), _p(p), _I64(K), _p(g), _I64(K), _p(w), _I64(K),
+                _p(row_exp[a:b]), _p(col_exp), _p(rm), _p(cm), _p(None if v_row is None else v_row[a:b]),
+                _p(v_col), _p(sum_v_inv), _p(cp), _I64(K), ctypes.c_float(lr), ctypes.c_float(eps),
+                _I32(salt), _I64(b - a), _I64(K), _I64(row0 + a), None)
+        ths.append(threading.Thread(target=work))
+    for t in ths:
+        t.start()
+    for t in ths:
+        t.join()
+    if col_max is not None:
+        np.maximum.reduce([col_max] + cms, out=col_max)
