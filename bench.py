@@ -153,6 +153,7 @@ def bench_ours(args, rank, world, device):
     torch.cuda.synchronize()
     clocks = ClockSampler(torch.cuda.current_device())
     clocks.start()
+    time.sleep(1.5)   # let nvidia-smi start before the timed launches
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
     for i in range(args.steps):

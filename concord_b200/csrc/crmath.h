@@ -21,9 +21,15 @@
 
 #if defined(__CUDACC__)
 #define CR_HD __host__ __device__ __forceinline__
+#define CR_SLOW static __host__ __device__ __noinline__
+#define CR_TABLE static __device__ const
 #else
 #define CR_HD static inline
+#define CR_SLOW static
+#define CR_TABLE static const
 #endif
+
+#include "crmath_tables.h"
 
 namespace crmath {
 
@@ -53,6 +59,15 @@ CR_HD float u2f(uint32_t u) {
     return __uint_as_float(u);
 #else
     float f; memcpy(&f, &u, 4); return f;
+#endif
+}
+
+// table read (read-only data cache on the GPU)
+CR_HD double tab(const double* t, int i) {
+#if defined(__CUDA_ARCH__)
+    return __ldg(t + i);
+#else
+    return t[i];
 #endif
 }
 
@@ -137,7 +152,7 @@ CR_HD void log_reduce(float x, float* m_out, int* e_out) {
 }
 
 // log(m) = 2 s (1 + z/3 + z^2/5 + ...), s = (m-1)/(m+1), z = s^2, |z| < 0.0295
-CR_HD float log2f_slow(float m, int e) {
+CR_SLOW float log2f_slow(float m, int e) {
     double md = (double)m;
     double num = md - 1.0, den = md + 1.0;  // exact
     double sh = num / den;
@@ -163,39 +178,53 @@ CR_HD float cr_log2f(float x) {
         return NAN;  // negative or NaN
     }
     if (x == INFINITY) return INFINITY;
+    // x = 2^k * z, z in [0.699, 1.398); sub-interval i of z has center 1/invc
+    uint32_t ix = f2u(x);
+    int kadj = 0;
+    if (ix < 0x00800000u) {  // subnormal: scale by 2^23 (exact)
+        ix = f2u(x * 8388608.0f);
+        kadj = -23;
+    }
+    const uint32_t tmp = ix - CR_LOG_OFF;
+    const int i = (int)((tmp >> 16) & 127u);
+    const int k = ((int32_t)tmp >> 23) + kadj;
+    const float z = u2f(ix - (tmp & 0xff800000u));
+    const double r = (double)z * tab(cr_log_invc, i) - 1.0;  // exact
+    // log2(1+r), |r| < 2^-7, degree 9 (relative error < 2^-60)
+    double p = CR_LOG_C8;
+    p = fma(p, r, CR_LOG_C7);
+    p = fma(p, r, CR_LOG_C6);
+    p = fma(p, r, CR_LOG_C5);
+    p = fma(p, r, CR_LOG_C4);
+    p = fma(p, r, CR_LOG_C3);
+    p = fma(p, r, CR_LOG_C2);
+    p = fma(p, r, CR_LOG_C1);
+    p = fma(p, r, CR_LOG_C0);
+    const double hi = (double)k + tab(cr_log_logc_hi, i);
+    const double L = hi + fma(p, r, tab(cr_log_logc_lo, i));
+    const double err = fabs(L) * 0x1p-46;
+    const float a = (float)(L + err), b = (float)(L - err);
+    if (!FORCE_SLOW && a == b) return a;
     float m; int e;
     log_reduce(x, &m, &e);
-    double md = (double)m;
-    double s = (md - 1.0) / (md + 1.0);
-    double z = s * s;
-    double p = 1.0 / 21.0;
-    p = fma(p, z, 1.0 / 19.0);
-    p = fma(p, z, 1.0 / 17.0);
-    p = fma(p, z, 1.0 / 15.0);
-    p = fma(p, z, 1.0 / 13.0);
-    p = fma(p, z, 1.0 / 11.0);
-    p = fma(p, z, 1.0 / 9.0);
-    p = fma(p, z, 1.0 / 7.0);
-    p = fma(p, z, 1.0 / 5.0);
-    p = fma(p, z, 1.0 / 3.0);
-    p = fma(p, z, 1.0);
-    double l2 = (2.0 * s) * p * CR_INVLN2_HI;
-    double L = (double)e + l2;
-    double err = fabs(L) * 0x1p-46;
-    float a = (float)(L + err), b = (float)(L - err);
-    if (!FORCE_SLOW && a == b) return a;
     return log2f_slow(m, e);
 }
 
-// 2^f for |f| <= 1/2 in double-double: exp(t), t = f ln2, Taylor to t^24/24!
+// 2^f for -1/128 <= f < 1 in double-double: exp(t), t = f ln2, Taylor to t^30/30!
 CR_HD dd exp2_frac_dd(double f) {
     dd t = dd_mul_d(dd{CR_LN2_HI, CR_LN2_LO}, f);
     dd sum = dd{1.0, 0.0}, term = dd{1.0, 0.0};
-    for (int k = 1; k <= 24; ++k) {
+    for (int k = 1; k <= 30; ++k) {
         term = dd_div_d(dd_mul(term, t), (double)k);
         sum = dd_add(sum, term);
     }
     return sum;
+}
+
+CR_SLOW float exp2f_slow(double f, double sc) {
+    dd v = exp2_frac_dd(f);
+    v.hi *= sc; v.lo *= sc;  // exact scaling by a power of two
+    return dd_to_float(v);
 }
 
 template <bool FORCE_SLOW = false>
@@ -203,35 +232,26 @@ CR_HD float cr_exp2f(float y) {
     if (y != y) return y;
     if (y >= 128.0f) return INFINITY;
     if (y < -150.0f) return 0.0f;
-    double yd = (double)y;
-    double n = rint(yd);
-    double f = yd - n;  // exact, |f| <= 1/2
-    int ni = (int)n;
-    if (f == 0.0) return (float)pow2d(ni);  // exact power of two (subnormals included)
-    double t = f * CR_LN2_HI;
-    double p = 1.0 / 87178291200.0;               // 1/14!
-    p = fma(p, t, 1.0 / 6227020800.0);            // 1/13!
-    p = fma(p, t, 1.0 / 479001600.0);             // 1/12!
-    p = fma(p, t, 1.0 / 39916800.0);
-    p = fma(p, t, 1.0 / 3628800.0);
-    p = fma(p, t, 1.0 / 362880.0);
-    p = fma(p, t, 1.0 / 40320.0);
-    p = fma(p, t, 1.0 / 5040.0);
-    p = fma(p, t, 1.0 / 720.0);
-    p = fma(p, t, 1.0 / 120.0);
-    p = fma(p, t, 1.0 / 24.0);
-    p = fma(p, t, 1.0 / 6.0);
-    p = fma(p, t, 0.5);
-    p = fma(p, t, 1.0);
-    p = fma(p, t, 1.0);
-    double sc = pow2d(ni);
-    double r = p * sc;
-    double err = r * 0x1p-46;
-    float a = (float)(r + err), b = (float)(r - err);
+    // y = n + j/64 + f, |f| <= 1/128; 2^y = 2^n * 2^(j/64) * 2^f
+    const float k64 = rintf(y * 64.0f);        // exact scaling, integer result
+    const int k = (int)k64;
+    const int j = k & 63, n = k >> 6;
+    const double f = (double)y - (double)k64 * 0.015625;  // exact
+    if (f == 0.0 && j == 0) return (float)pow2d(n);     // exact power of two
+    double p = CR_EXP_C7;
+    p = fma(p, f, CR_EXP_C6);
+    p = fma(p, f, CR_EXP_C5);
+    p = fma(p, f, CR_EXP_C4);
+    p = fma(p, f, CR_EXP_C3);
+    p = fma(p, f, CR_EXP_C2);
+    p = fma(p, f, CR_EXP_C1);
+    const double t = tab(cr_exp2_tab_hi, j);
+    const double sc = pow2d(n);
+    const double rr = fma(t * f, p, t) * sc;  // t * (1 + f p)
+    const double err = rr * 0x1p-46;
+    const float a = (float)(rr + err), b = (float)(rr - err);
     if (!FORCE_SLOW && a == b) return a;
-    dd v = exp2_frac_dd(f);
-    v.hi *= sc; v.lo *= sc;  // exact scaling by a power of two
-    return dd_to_float(v);
+    return exp2f_slow((double)y - (double)n, sc);
 }
 
 }  // namespace crmath

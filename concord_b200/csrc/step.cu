@@ -10,6 +10,8 @@
 // (col_exp, v_col) stays in registers, reduces |m_eff| per row with warp
 // shuffles and per column through shared memory, and issues one atomicMax
 // per (row, warp) and per (column, block).
+#include <stdlib.h>
+
 #include "common.cuh"
 
 namespace concord {
@@ -27,11 +29,24 @@ struct ElemOut {
     float coh_pre;  // updated coh_pre (when written)
 };
 
+// Flag sets with their own kernel instantiation; anything else runs the
+// instantiation that reads the flags at run time (FL_DYNAMIC).
+constexpr uint32_t FL_DYNAMIC = 0x80000000u;
+constexpr uint32_t FL_BARE = CONCORD_F_MASS_PRESERVE | CONCORD_F_APPLY_CHASE | CONCORD_F_TRACK_REBALANCE |
+                             CONCORD_F_GF_TRUST | CONCORD_F_COHPRE | CONCORD_F_FIXED_COH;
+constexpr uint32_t FL_NOCOHPRE = FL_BARE & ~CONCORD_F_COHPRE;
+
+template <uint32_t FL>
+__device__ __forceinline__ uint32_t flags_of(const concord_step_params& P) {
+    return (FL & FL_DYNAMIC) ? P.flags : FL;
+}
+
 // One element of the AdamW-path step (packed_b.py:476-703).
+template <uint32_t FL>
 __device__ __forceinline__ ElemOut step_adamw(const concord_step_params& P, int32_t packed, float g,
                                               int32_t row_e, int32_t col_e, float v_row, float v_col,
                                               float cp, const StepScalars& S, int32_t pos) {
-    const uint32_t F = P.flags;
+    const uint32_t F = flags_of<FL>(P);
     int32_t s_fast = packed >> 16;
     int32_t s_slow = shl32(packed, 16) >> 24;
     int32_t v_slow = shl32(packed, 24) >> 24;
@@ -130,6 +145,7 @@ __device__ __forceinline__ ElemOut step_adamw(const concord_step_params& P, int3
 }
 
 // One element of the SGD-path step (packed_b.py:214-312).
+template <uint32_t FL>
 __device__ __forceinline__ ElemOut step_sgd(const concord_step_params& P, int32_t packed, float g,
                                             int32_t row_e, int32_t col_e, const StepScalars& S,
                                             int32_t pos) {
@@ -149,7 +165,7 @@ __device__ __forceinline__ ElemOut step_sgd(const concord_step_params& P, int32_
     float delta_v8 = P.alpha_v_fast * (float)(s_slow * 128 - v_slow * 128) / 128.0f;
     int32_t tv = sr_tick(delta_v8, hash_uniform(s_fast, pos, S.salt ^ 0x33335555));
     int32_t new_v = clampi(v_slow + tv, -128, 127);
-    if (P.flags & CONCORD_F_MASS_PRESERVE) s_slow = s_slow - (new_v - v_slow);
+    if (flags_of<FL>(P) & CONCORD_F_MASS_PRESERVE) s_slow = s_slow - (new_v - v_slow);
 
     int32_t sfc = clampi(s_fast, -32768, 32767);
     int32_t ssc = clampi(s_slow, -128, 127);
@@ -191,9 +207,11 @@ __device__ __forceinline__ StepScalars load_scalars(const StepArgs& A) {
 
 namespace concord {
 
+
 constexpr int STEP_THREADS = 256;
-constexpr int STEP_COLS = 256;  // 32 lanes x 8 columns
-constexpr int STEP_ROWS = 32;   // rows per block (4 per warp)
+constexpr int VEC = 4;                 // consecutive columns per thread
+constexpr int STEP_COLS = 32 * VEC;    // columns per block (one warp-width)
+constexpr int STEP_ROWS = 64;          // rows per block (8 per warp)
 
 __device__ __forceinline__ void block_add_coh(double csum, double ccnt, double* coh_stats) {
     __shared__ double red[2][STEP_THREADS / 32];
@@ -212,14 +230,23 @@ __device__ __forceinline__ void block_add_coh(double csum, double ccnt, double* 
     }
 }
 
-// Vector path: K % 8 == 0, row strides % 8 == 0, 16-byte aligned bases.
-template <int KIND>
-__global__ void __launch_bounds__(STEP_THREADS) step_vec_kernel(StepArgs A) {
+template <int KIND, uint32_t FL>
+__device__ __forceinline__ ElemOut step_elem(const concord_step_params& P, int32_t w, float g, int32_t re,
+                                             int32_t ce, float vr, float vc, float cp,
+                                             const StepScalars& S, int32_t pos) {
+    if (KIND == CONCORD_KIND_ADAMW) return step_adamw<FL>(P, w, g, re, ce, vr, vc, cp, S, pos);
+    return step_sgd<FL>(P, w, g, re, ce, S, pos);
+}
+
+// Vector path: K % 4 == 0, row strides % 4 == 0, 16-byte aligned bases.
+// Block = 8 warps; each warp covers 128 columns (4 per lane) of 8 rows.
+template <int KIND, uint32_t FL, int MINB>
+__global__ void __launch_bounds__(STEP_THREADS, MINB) step_vec_kernel(StepArgs A) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int64_t k0 = (int64_t)blockIdx.x * STEP_COLS + lane * 8;
+    const int64_t k0 = (int64_t)blockIdx.x * STEP_COLS + lane * VEC;
     const bool active = k0 < A.K;
     const int64_t rbase = (int64_t)blockIdx.y * STEP_ROWS;
-    const uint32_t F = A.P.flags;
+    const uint32_t F = flags_of<FL>(A.P);
     const bool adamw = KIND == CONCORD_KIND_ADAMW;
     const bool need_vhat = adamw && (F & (CONCORD_F_GF_TRUST | CONCORD_F_GF_CONSOL | CONCORD_F_COHPRE | CONCORD_F_RATIO_COH));
     const bool need_coh = adamw && (F & (CONCORD_F_GF_CONSOL | CONCORD_F_COHPRE | CONCORD_F_RATIO_COH));
@@ -228,71 +255,58 @@ __global__ void __launch_bounds__(STEP_THREADS) step_vec_kernel(StepArgs A) {
     const bool track = (F & CONCORD_F_TRACK_REBALANCE) != 0;
     const StepScalars S = load_scalars(A);
 
-    int32_t ce[8];
-    float vc[8];
-    int cmx[8];
+    int32_t ce[VEC];
+    float vc[VEC];
+    int cmx[VEC];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) { ce[j] = 0; vc[j] = 0.0f; cmx[j] = 0; }
+    for (int j = 0; j < VEC; ++j) { ce[j] = 0; vc[j] = 0.0f; cmx[j] = 0; }
     if (active) {
-        int2 c8 = *reinterpret_cast<const int2*>(A.col_exp + k0);
-        const int8_t* cb = reinterpret_cast<const int8_t*>(&c8);
+        const uint32_t c4 = *reinterpret_cast<const uint32_t*>(A.col_exp + k0);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) ce[j] = cb[j];
+        for (int j = 0; j < VEC; ++j) ce[j] = (int32_t)(int8_t)(c4 >> (8 * j));
         if (need_vhat) {
-            float4 a = *reinterpret_cast<const float4*>(A.v_col + k0);
-            float4 b = *reinterpret_cast<const float4*>(A.v_col + k0 + 4);
+            float4 a = __ldg(reinterpret_cast<const float4*>(A.v_col + k0));
             vc[0] = a.x; vc[1] = a.y; vc[2] = a.z; vc[3] = a.w;
-            vc[4] = b.x; vc[5] = b.y; vc[6] = b.z; vc[7] = b.w;
         }
     }
-    double csum = 0.0, ccnt = 0.0;
+    double csum = 0.0;
+    int ccnt = 0;
     for (int r = warp; r < STEP_ROWS; r += STEP_THREADS / 32) {
         const int64_t n = rbase + r;
         if (n >= A.N) break;
         int rml = 0;
         if (active) {
             const int32_t re = A.row_exp[n];
-            const float vr = need_vhat ? A.v_row[n] : 0.0f;
+            const float vr = need_vhat ? __ldg(A.v_row + n) : 0.0f;
             int32_t* pw = A.packed + n * A.ldp + k0;
-            int4 w0 = *reinterpret_cast<const int4*>(pw);
-            int4 w1 = *reinterpret_cast<const int4*>(pw + 4);
-            uint4 g8 = __ldg(reinterpret_cast<const uint4*>(A.grad + n * A.ldg + k0));
-            float cp[8];
+            int4 w4 = __ldcs(reinterpret_cast<const int4*>(pw));
+            uint2 g4 = __ldcs(reinterpret_cast<const uint2*>(A.grad + n * A.ldg + k0));
+            float cp[VEC] = {1.0f, 1.0f, 1.0f, 1.0f};
+            float* pc = use_cp ? A.coh_pre + n * A.ldc + k0 : nullptr;
             if (use_cp) {
-                const float* pc = A.coh_pre + n * A.ldc + k0;
-                float4 a = *reinterpret_cast<const float4*>(pc);
-                float4 b = *reinterpret_cast<const float4*>(pc + 4);
+                float4 a = __ldcs(reinterpret_cast<const float4*>(pc));
                 cp[0] = a.x; cp[1] = a.y; cp[2] = a.z; cp[3] = a.w;
-                cp[4] = b.x; cp[5] = b.y; cp[6] = b.z; cp[7] = b.w;
-            } else {
-#pragma unroll
-                for (int j = 0; j < 8; ++j) cp[j] = 1.0f;
             }
-            int32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-            uint32_t gw[4] = {g8.x, g8.y, g8.z, g8.w};
-            uint32_t ob[4];
+            int32_t wv[VEC] = {w4.x, w4.y, w4.z, w4.w};
+            const uint32_t gw[2] = {g4.x, g4.y};
+            uint32_t ob[2];
             const int32_t posn = shl32((int32_t)(A.row0 + n), 16);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
+            for (int j = 0; j < VEC; ++j) {
                 const float g = bf16_to_f32((gw[j >> 1] >> ((j & 1) * 16)) & 0xffffu);
                 const int32_t pos = posn ^ (int32_t)(k0 + j);
-                ElemOut o = adamw ? step_adamw(A.P, wv[j], g, re, ce[j], vr, vc[j], cp[j], S, pos)
-                                  : step_sgd(A.P, wv[j], g, re, ce[j], S, pos);
+                ElemOut o = step_elem<KIND, FL>(A.P, wv[j], g, re, ce[j], vr, vc[j], cp[j], S, pos);
                 wv[j] = o.word;
                 cp[j] = o.coh_pre;
                 if (j & 1) ob[j >> 1] |= (uint32_t)o.wbits << 16; else ob[j >> 1] = o.wbits;
                 rml = max(rml, o.abs_eff);
                 cmx[j] = max(cmx[j], o.abs_eff);
-                if (need_coh) { csum += (double)o.coh; ccnt += 1.0; }
+                if (need_coh) csum += (double)o.coh;
             }
-            *reinterpret_cast<int4*>(pw) = make_int4(wv[0], wv[1], wv[2], wv[3]);
-            *reinterpret_cast<int4*>(pw + 4) = make_int4(wv[4], wv[5], wv[6], wv[7]);
-            *reinterpret_cast<uint4*>(A.wbuf + n * A.ldw + k0) = make_uint4(ob[0], ob[1], ob[2], ob[3]);
-            if (write_cp) {
-                float* pc = A.coh_pre + n * A.ldc + k0;
-                *reinterpret_cast<float4*>(pc) = make_float4(cp[0], cp[1], cp[2], cp[3]);
-                *reinterpret_cast<float4*>(pc + 4) = make_float4(cp[4], cp[5], cp[6], cp[7]);
-            }
+            if (need_coh) ccnt += VEC;
+            __stcs(reinterpret_cast<int4*>(pw), make_int4(wv[0], wv[1], wv[2], wv[3]));
+            __stcs(reinterpret_cast<uint2*>(A.wbuf + n * A.ldw + k0), make_uint2(ob[0], ob[1]));
+            if (write_cp) __stcs(reinterpret_cast<float4*>(pc), make_float4(cp[0], cp[1], cp[2], cp[3]));
         }
         if (track) {
             int m = warp_max(rml);
@@ -302,18 +316,20 @@ __global__ void __launch_bounds__(STEP_THREADS) step_vec_kernel(StepArgs A) {
     if (track) {
         __shared__ int cm[STEP_THREADS / 32][STEP_COLS];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) cm[warp][lane * 8 + j] = cmx[j];
+        for (int j = 0; j < VEC; ++j) cm[warp][lane * VEC + j] = cmx[j];
         __syncthreads();
-        int m = 0;
+        if (threadIdx.x < STEP_COLS) {
+            int m = 0;
 #pragma unroll
-        for (int w = 0; w < STEP_THREADS / 32; ++w) m = max(m, cm[w][threadIdx.x]);
-        const int64_t col = (int64_t)blockIdx.x * STEP_COLS + threadIdx.x;
-        if (col < A.K && m > 0) atomicMax(A.col_max + col, m);
+            for (int w = 0; w < STEP_THREADS / 32; ++w) m = max(m, cm[w][threadIdx.x]);
+            const int64_t col = (int64_t)blockIdx.x * STEP_COLS + threadIdx.x;
+            if (col < A.K && m > 0) atomicMax(A.col_max + col, m);
+        }
     }
-    if (need_coh && A.coh_stats) block_add_coh(csum, ccnt, A.coh_stats);
+    if (need_coh && A.coh_stats) block_add_coh(csum, (double)ccnt, A.coh_stats);
 }
 
-// Generic path: any K and strides, one element per thread.
+// Generic path: any K and strides, one element per thread (runtime flags).
 template <int KIND>
 __global__ void __launch_bounds__(STEP_THREADS) step_generic_kernel(StepArgs A) {
     const uint32_t F = A.P.flags;
@@ -332,10 +348,9 @@ __global__ void __launch_bounds__(STEP_THREADS) step_generic_kernel(StepArgs A) 
         const int32_t pos = shl32((int32_t)(A.row0 + n), 16) ^ (int32_t)k;
         const float g = bf16_to_f32(A.grad[n * A.ldg + k]);
         const float cp = use_cp ? A.coh_pre[n * A.ldc + k] : 1.0f;
-        ElemOut o = adamw ? step_adamw(A.P, A.packed[n * A.ldp + k], g, A.row_exp[n], A.col_exp[k],
-                                       need_vhat ? A.v_row[n] : 0.0f, need_vhat ? A.v_col[k] : 0.0f,
-                                       cp, S, pos)
-                          : step_sgd(A.P, A.packed[n * A.ldp + k], g, A.row_exp[n], A.col_exp[k], S, pos);
+        ElemOut o = step_elem<KIND, FL_DYNAMIC>(A.P, A.packed[n * A.ldp + k], g, A.row_exp[n], A.col_exp[k],
+                                                need_vhat ? A.v_row[n] : 0.0f, need_vhat ? A.v_col[k] : 0.0f,
+                                                cp, S, pos);
         A.packed[n * A.ldp + k] = o.word;
         A.wbuf[n * A.ldw + k] = o.wbits;
         if (write_cp) A.coh_pre[n * A.ldc + k] = o.coh_pre;
@@ -346,6 +361,14 @@ __global__ void __launch_bounds__(STEP_THREADS) step_generic_kernel(StepArgs A) 
         if (need_coh) { csum += (double)o.coh; ccnt += 1.0; }
     }
     if (need_coh && A.coh_stats) block_add_coh(csum, ccnt, A.coh_stats);
+}
+
+template <int MINB>
+static void launch_vec(bool adamw, uint32_t F, bool has_cp, dim3 grid, cudaStream_t s, const StepArgs& A) {
+    if (!adamw) step_vec_kernel<CONCORD_KIND_SGD, FL_DYNAMIC, MINB><<<grid, STEP_THREADS, 0, s>>>(A);
+    else if (F == FL_BARE && has_cp) step_vec_kernel<CONCORD_KIND_ADAMW, FL_BARE, MINB><<<grid, STEP_THREADS, 0, s>>>(A);
+    else if (F == FL_NOCOHPRE) step_vec_kernel<CONCORD_KIND_ADAMW, FL_NOCOHPRE, MINB><<<grid, STEP_THREADS, 0, s>>>(A);
+    else step_vec_kernel<CONCORD_KIND_ADAMW, FL_DYNAMIC, MINB><<<grid, STEP_THREADS, 0, s>>>(A);
 }
 
 }  // namespace concord
@@ -367,28 +390,32 @@ extern "C" int concord_step(const concord_step_params* p, int32_t* packed, int64
         return fail(CONCORD_EINVAL, "concord_step: optimizer kind must be adamw or sgd");
     const uint32_t F = p->flags;
     const bool adamw = p->kind == CONCORD_KIND_ADAMW;
+    const bool need_vhat = adamw && (F & (CONCORD_F_GF_TRUST | CONCORD_F_GF_CONSOL | CONCORD_F_COHPRE | CONCORD_F_RATIO_COH));
     if (adamw && !eps) return fail(CONCORD_EINVAL, "concord_step: eps is required for adamw");
-    if (adamw && (F & (CONCORD_F_GF_TRUST | CONCORD_F_GF_CONSOL | CONCORD_F_COHPRE | CONCORD_F_RATIO_COH)) &&
-        (!v_row || !v_col || !sum_v_inv))
+    if (need_vhat && (!v_row || !v_col || !sum_v_inv))
         return fail(CONCORD_EINVAL, "concord_step: gf_trust/gf_consol/coh_pre/ratio need v_row, v_col, sum_v_inv");
     if ((F & CONCORD_F_TRACK_REBALANCE) && (!row_max || !col_max))
         return fail(CONCORD_EINVAL, "concord_step: track_rebalance needs row_max and col_max");
-    if (adamw && (F & CONCORD_F_COHPRE) && !(F & CONCORD_F_RATIO_COH) && coh_pre && ldc < K)
-        return fail(CONCORD_ESHAPE, "concord_step: bad coh_pre stride");
+    const bool use_cp = adamw && (F & CONCORD_F_COHPRE) && !(F & CONCORD_F_RATIO_COH) && coh_pre;
+    if (use_cp && ldc < K) return fail(CONCORD_ESHAPE, "concord_step: bad coh_pre stride");
     if (row0 < 0 || row0 + N > (int64_t)1 << 31) return fail(CONCORD_ESHAPE, "concord_step: row index beyond int32");
     StepArgs A{*p, packed, ldp, grad, ldg, wbuf, ldw, row_exp, col_exp, row_max, col_max,
                v_row, v_col, sum_v_inv, coh_pre, ldc, lr, eps, salt, N, K, row0, coh_stats};
-    bool vec = (K % 8 == 0) && (ldp % 8 == 0) && (ldg % 8 == 0) && (ldw % 8 == 0) &&
-               aligned(packed, 16) && aligned(grad, 16) && aligned(wbuf, 16) && aligned(col_exp, 8);
-    if (adamw && (F & (CONCORD_F_GF_TRUST | CONCORD_F_GF_CONSOL | CONCORD_F_COHPRE | CONCORD_F_RATIO_COH)))
-        vec = vec && aligned(v_col, 16);
-    if (coh_pre) vec = vec && (ldc % 8 == 0) && aligned(coh_pre, 16);
+    bool vec = (K % VEC == 0) && (ldp % VEC == 0) && (ldg % VEC == 0) && (ldw % VEC == 0) &&
+               aligned(packed, 16) && aligned(grad, 8) && aligned(wbuf, 8) && aligned(col_exp, 4);
+    if (need_vhat) vec = vec && aligned(v_col, 16);
+    if (use_cp) vec = vec && (ldc % VEC == 0) && aligned(coh_pre, 16);
     cudaStream_t s = as_stream(stream);
     if (vec) {
         dim3 grid((unsigned)((K + STEP_COLS - 1) / STEP_COLS), (unsigned)((N + STEP_ROWS - 1) / STEP_ROWS));
         if (grid.y > 65535) return fail(CONCORD_ETOOBIG, "concord_step: too many rows for one launch");
-        if (adamw) step_vec_kernel<CONCORD_KIND_ADAMW><<<grid, STEP_THREADS, 0, s>>>(A);
-        else step_vec_kernel<CONCORD_KIND_SGD><<<grid, STEP_THREADS, 0, s>>>(A);
+        // resident blocks per SM the register budget is tuned for (CONCORD_STEP_MINB=2|3)
+        static const int minb = [] {
+            const char* e = getenv("CONCORD_STEP_MINB");
+            return (e && e[0] == '2') ? 2 : 3;
+        }();
+        if (minb == 2) launch_vec<2>(adamw, F, coh_pre != nullptr, grid, s, A);
+        else launch_vec<3>(adamw, F, coh_pre != nullptr, grid, s, A);
     } else {
         int64_t blocks = (N * K + STEP_THREADS - 1) / STEP_THREADS;
         if (blocks > 148 * 64) blocks = 148 * 64;
