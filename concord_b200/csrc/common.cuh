@@ -34,6 +34,11 @@ __device__ __forceinline__ float np_min(float a, float b) {
     return a < b ? a : b;
 }
 
+// numpy minimum(maximum(x, -cap), cap) for a finite cap: a NaN x propagates
+__device__ __forceinline__ float clamp_np(float x, float cap) {
+    return x != x ? x : fminf(fmaxf(x, -cap), cap);
+}
+
 __device__ __forceinline__ int32_t clampi(int32_t v, int32_t lo, int32_t hi) {
     return v < lo ? lo : (v > hi ? hi : v);
 }

@@ -23,7 +23,9 @@
 #define CR_HD __host__ __device__ __forceinline__
 #define CR_SLOW static __host__ __device__ __noinline__
 #define CR_TABLE static __device__ const
+#define CR_ALIGN16 __align__(16)
 #else
+#define CR_ALIGN16 alignas(16)
 #define CR_HD static inline
 #define CR_SLOW static
 #define CR_TABLE static const
@@ -76,6 +78,16 @@ CR_HD double pow2d(int n) { return u2d((uint64_t)(int64_t)(n + 1023) << 52); }
 
 // ---- double-double arithmetic (value = hi + lo, |lo| <= ulp(hi)/2) ----
 struct dd { double hi, lo; };
+
+// (hi, lo) pair i of a table of double-doubles, in one 16-byte load
+CR_HD dd tab2(const double* t, int i) {
+#if defined(__CUDA_ARCH__)
+    const double2 v = __ldg(reinterpret_cast<const double2*>(t) + i);
+    return dd{v.x, v.y};
+#else
+    return dd{t[2 * i], t[2 * i + 1]};
+#endif
+}
 
 CR_HD dd quick_two_sum(double a, double b) { double s = a + b; return {s, b - (s - a)}; }
 CR_HD dd two_sum(double a, double b) {
@@ -171,8 +183,11 @@ CR_SLOW float log2f_slow(float m, int e) {
     return dd_to_float(L);
 }
 
-template <bool FORCE_SLOW = false>
-CR_HD float cr_log2f(float x) {
+// Full-range log2 (zero, negative, NaN, inf, subnormals) with a float-compare
+// rounding test; reached from cr_log2f only for special inputs or when the
+// fast path cannot decide the rounding.
+template <bool FORCE_SLOW>
+CR_SLOW float log2f_careful(float x) {
     if (!(x > 0.0f)) {
         if (x == 0.0f) return -INFINITY;
         return NAN;  // negative or NaN
@@ -200,8 +215,8 @@ CR_HD float cr_log2f(float x) {
     p = fma(p, r, CR_LOG_C2);
     p = fma(p, r, CR_LOG_C1);
     p = fma(p, r, CR_LOG_C0);
-    const double hi = (double)k + tab(cr_log_logc_hi, i);
-    const double L = hi + fma(p, r, tab(cr_log_logc_lo, i));
+    const dd lc = tab2(cr_log_logc, i);
+    const double L = ((double)k + lc.hi) + fma(p, r, lc.lo);
     const double err = fabs(L) * 0x1p-46;
     const float a = (float)(L + err), b = (float)(L - err);
     if (!FORCE_SLOW && a == b) return a;
@@ -227,8 +242,8 @@ CR_SLOW float exp2f_slow(double f, double sc) {
     return dd_to_float(v);
 }
 
-template <bool FORCE_SLOW = false>
-CR_HD float cr_exp2f(float y) {
+template <bool FORCE_SLOW>
+CR_SLOW float exp2f_careful(float y) {
     if (y != y) return y;
     if (y >= 128.0f) return INFINITY;
     if (y < -150.0f) return 0.0f;
@@ -252,6 +267,65 @@ CR_HD float cr_exp2f(float y) {
     const float a = (float)(rr + err), b = (float)(rr - err);
     if (!FORCE_SLOW && a == b) return a;
     return exp2f_slow((double)y - (double)n, sc);
+}
+
+// True when the double v lies within 2^8 double ulps of a midpoint between
+// two adjacent floats (only meaningful when (float)v is a normal float).
+CR_HD bool near_float_midpoint(double v) {
+    const uint32_t t = (uint32_t)d2u(v) & 0x1FFFFFFFu;   // the 29 bits below float precision
+    return (uint32_t)(t - 0x10000000u + 0x100u) <= 0x200u;
+}
+
+// Correctly rounded log2 of an fp32 value.  Hot path: normal positive x,
+// x = 2^k z, z*invc - 1 = r exact, log2(1+r) by a degree-7 polynomial in
+// double (relative error < 2^-50); the bits test sends the rare ambiguous
+// roundings (and every special input) to log2f_careful.
+template <bool FORCE_SLOW = false>
+CR_HD float cr_log2f(float x) {
+    const uint32_t ix = f2u(x);
+    if (FORCE_SLOW || ix - 0x00800000u >= 0x7F000000u) return log2f_careful<FORCE_SLOW>(x);
+    const uint32_t tmp = ix - CR_LOG_OFF;
+    const int i = (int)((tmp >> 16) & 127u);
+    const int k = (int32_t)tmp >> 23;
+    const float z = u2f(ix - (tmp & 0xff800000u));
+    const double r = (double)z * tab(cr_log_invc, i) - 1.0;  // exact
+    double p = CR_LOG_C6;
+    p = fma(p, r, CR_LOG_C5);
+    p = fma(p, r, CR_LOG_C4);
+    p = fma(p, r, CR_LOG_C3);
+    p = fma(p, r, CR_LOG_C2);
+    p = fma(p, r, CR_LOG_C1);
+    p = fma(p, r, CR_LOG_C0);
+    const dd lc = tab2(cr_log_logc, i);
+    const double L = ((double)k + lc.hi) + fma(p, r, lc.lo);
+    if (near_float_midpoint(L)) return log2f_careful<false>(x);
+    return (float)L;
+}
+
+// Correctly rounded 2^y for fp32 y.  Hot path: -126 <= y < 128 (normal
+// result): y = (n*64 + j)/64 + f, |f| <= 1/128, 2^y = 2^n 2^(j/64) (1 + q(f)),
+// q of degree 6 (relative error < 2^-50); 2^n enters the exponent field.
+template <bool FORCE_SLOW = false>
+CR_HD float cr_exp2f(float y) {
+    if (FORCE_SLOW || !(y >= -126.0f && y < 128.0f)) return exp2f_careful<FORCE_SLOW>(y);
+    const float t = y * 64.0f + 12582912.0f;          // 1.5 * 2^23: rounds y*64 to an integer
+    const int k = (int)(f2u(t) - 0x4B400000u);
+    const float k64 = t - 12582912.0f;
+    const float f = y - k64 * 0.015625f;               // exact, |f| <= 1/128
+    const int j = k & 63, n = k >> 6;
+    const double fd = (double)f;
+    double q = CR_EXP_C6;
+    q = fma(q, fd, CR_EXP_C5);
+    q = fma(q, fd, CR_EXP_C4);
+    q = fma(q, fd, CR_EXP_C3);
+    q = fma(q, fd, CR_EXP_C2);
+    q = fma(q, fd, CR_EXP_C1);
+    q = q * fd;
+    const double T = tab(cr_exp2_tab_hi, j);
+    double rr = fma(T, q, T);
+    rr = u2d(d2u(rr) + ((uint64_t)(int64_t)n << 52));  // * 2^n
+    if (near_float_midpoint(rr)) return exp2f_careful<false>(y);
+    return (float)rr;
 }
 
 }  // namespace crmath

@@ -12,6 +12,8 @@
 // per (row, warp) and per (column, block).
 #include <stdlib.h>
 
+#include <cuda_bf16.h>
+
 #include "common.cuh"
 
 namespace concord {
@@ -23,7 +25,7 @@ struct StepScalars {
 
 struct ElemOut {
     int32_t word;
-    uint16_t wbits;
+    float wval;     // new live weight (fp32; stored as bf16)
     int32_t abs_eff;
     float coh;      // valid when the flags compute coh
     float coh_pre;  // updated coh_pre (when written)
@@ -77,12 +79,14 @@ __device__ __forceinline__ ElemOut step_adamw(const concord_step_params& P, int3
             float mg = P.alpha_v_fast * d_sv * scale_fwd;
             coh = mg * mg / (v_hat + 1e-12f);
         }
-        coh = np_min(np_max(coh, 0.0f), 1.0f);
+        // with the fixed gate 0 <= sig2 <= den, so the clamp is the identity
+        // (a NaN propagates either way)
+        if (!(F & CONCORD_F_FIXED_COH)) coh = np_min(np_max(coh, 0.0f), 1.0f);
     }
 
     float denom_p = crmath::cr_exp2f(P.precond_p * crmath::cr_log2f(v_proxy + S.eps));
     float step_live = g / denom_p;
-    step_live = np_min(np_max(step_live, -P.step_cap), P.step_cap);
+    step_live = clamp_np(step_live, P.step_cap);
 
     const bool consol = (F & CONCORD_F_GF_CONSOL) != 0;
     float evap = 0.0f;
@@ -137,7 +141,7 @@ __device__ __forceinline__ ElemOut step_adamw(const concord_step_params& P, int3
     int32_t m_new = ssc * 128 + sfc + new_v * 128;
     ElemOut o;
     o.word = repack(sfc, ssc, new_v);
-    o.wbits = f32_to_bf16((float)m_new * scale_fwd);
+    o.wval = (float)m_new * scale_fwd;
     o.abs_eff = abs(m_new);
     o.coh = coh;
     o.coh_pre = cp_new;
@@ -172,7 +176,7 @@ __device__ __forceinline__ ElemOut step_sgd(const concord_step_params& P, int32_
     int32_t m_new = ssc * 128 + sfc + new_v * 128;
     ElemOut o;
     o.word = repack(sfc, ssc, new_v);
-    o.wbits = f32_to_bf16((float)m_new * exp2i(te));
+    o.wval = (float)m_new * exp2i(te);
     o.abs_eff = abs(m_new);
     o.coh = 0.0f;
     o.coh_pre = 1.0f;
@@ -269,7 +273,7 @@ __global__ void __launch_bounds__(STEP_THREADS, MINB) step_vec_kernel(StepArgs A
             vc[0] = a.x; vc[1] = a.y; vc[2] = a.z; vc[3] = a.w;
         }
     }
-    double csum = 0.0;
+    float csum = 0.0f;
     int ccnt = 0;
     for (int r = warp; r < STEP_ROWS; r += STEP_THREADS / 32) {
         const int64_t n = rbase + r;
@@ -289,7 +293,7 @@ __global__ void __launch_bounds__(STEP_THREADS, MINB) step_vec_kernel(StepArgs A
             }
             int32_t wv[VEC] = {w4.x, w4.y, w4.z, w4.w};
             const uint32_t gw[2] = {g4.x, g4.y};
-            uint32_t ob[2];
+            float wf[VEC];
             const int32_t posn = shl32((int32_t)(A.row0 + n), 16);
 #pragma unroll
             for (int j = 0; j < VEC; ++j) {
@@ -298,14 +302,17 @@ __global__ void __launch_bounds__(STEP_THREADS, MINB) step_vec_kernel(StepArgs A
                 ElemOut o = step_elem<KIND, FL>(A.P, wv[j], g, re, ce[j], vr, vc[j], cp[j], S, pos);
                 wv[j] = o.word;
                 cp[j] = o.coh_pre;
-                if (j & 1) ob[j >> 1] |= (uint32_t)o.wbits << 16; else ob[j >> 1] = o.wbits;
+                wf[j] = o.wval;
                 rml = max(rml, o.abs_eff);
                 cmx[j] = max(cmx[j], o.abs_eff);
-                if (need_coh) csum += (double)o.coh;
+                if (need_coh) csum += o.coh;
             }
             if (need_coh) ccnt += VEC;
             __stcs(reinterpret_cast<int4*>(pw), make_int4(wv[0], wv[1], wv[2], wv[3]));
-            __stcs(reinterpret_cast<uint2*>(A.wbuf + n * A.ldw + k0), make_uint2(ob[0], ob[1]));
+            __nv_bfloat162 b01 = __floats2bfloat162_rn(wf[0], wf[1]);
+            __nv_bfloat162 b23 = __floats2bfloat162_rn(wf[2], wf[3]);
+            __stcs(reinterpret_cast<uint2*>(A.wbuf + n * A.ldw + k0),
+                   make_uint2(*reinterpret_cast<uint32_t*>(&b01), *reinterpret_cast<uint32_t*>(&b23)));
             if (write_cp) __stcs(reinterpret_cast<float4*>(pc), make_float4(cp[0], cp[1], cp[2], cp[3]));
         }
         if (track) {
@@ -326,7 +333,7 @@ __global__ void __launch_bounds__(STEP_THREADS, MINB) step_vec_kernel(StepArgs A
             if (col < A.K && m > 0) atomicMax(A.col_max + col, m);
         }
     }
-    if (need_coh && A.coh_stats) block_add_coh(csum, (double)ccnt, A.coh_stats);
+    if (need_coh && A.coh_stats) block_add_coh((double)csum, (double)ccnt, A.coh_stats);
 }
 
 // Generic path: any K and strides, one element per thread (runtime flags).
@@ -352,7 +359,7 @@ __global__ void __launch_bounds__(STEP_THREADS) step_generic_kernel(StepArgs A) 
                                                 need_vhat ? A.v_row[n] : 0.0f, need_vhat ? A.v_col[k] : 0.0f,
                                                 cp, S, pos);
         A.packed[n * A.ldp + k] = o.word;
-        A.wbuf[n * A.ldw + k] = o.wbits;
+        A.wbuf[n * A.ldw + k] = __bfloat16_as_ushort(__float2bfloat16_rn(o.wval));
         if (write_cp) A.coh_pre[n * A.ldc + k] = o.coh_pre;
         if (track && o.abs_eff > 0) {
             atomicMax(A.row_max + n, o.abs_eff);
@@ -392,6 +399,7 @@ extern "C" int concord_step(const concord_step_params* p, int32_t* packed, int64
     const bool adamw = p->kind == CONCORD_KIND_ADAMW;
     const bool need_vhat = adamw && (F & (CONCORD_F_GF_TRUST | CONCORD_F_GF_CONSOL | CONCORD_F_COHPRE | CONCORD_F_RATIO_COH));
     if (adamw && !eps) return fail(CONCORD_EINVAL, "concord_step: eps is required for adamw");
+    if (p->step_cap != p->step_cap) return fail(CONCORD_EINVAL, "concord_step: step_cap is NaN");
     if (need_vhat && (!v_row || !v_col || !sum_v_inv))
         return fail(CONCORD_EINVAL, "concord_step: gf_trust/gf_consol/coh_pre/ratio need v_row, v_col, sum_v_inv");
     if ((F & CONCORD_F_TRACK_REBALANCE) && (!row_max || !col_max))

@@ -127,7 +127,7 @@ def test_step_matches_oracle_random(pb, oracle_mod, case, shape):
     s = stats.cpu().numpy()
     assert s[1] == ref_stats[1]
     if ref_stats[1] > 0:
-        assert abs(s[0] - ref_stats[0]) <= 1e-9 * max(1.0, abs(ref_stats[0]))
+        assert abs(s[0] - ref_stats[0]) <= 1e-5 * max(1.0, abs(ref_stats[0]))
 
 
 @pytest.mark.parametrize("shape", [(1, 1), (37, 70), (128, 256), (300, 1000), (1024, 1024),
