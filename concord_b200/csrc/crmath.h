@@ -289,13 +289,13 @@ CR_HD float cr_log2f(float x) {
     const int k = (int32_t)tmp >> 23;
     const float z = u2f(ix - (tmp & 0xff800000u));
     const double r = (double)z * tab(cr_log_invc, i) - 1.0;  // exact
-    double p = CR_LOG_C6;
-    p = fma(p, r, CR_LOG_C5);
-    p = fma(p, r, CR_LOG_C4);
-    p = fma(p, r, CR_LOG_C3);
-    p = fma(p, r, CR_LOG_C2);
-    p = fma(p, r, CR_LOG_C1);
-    p = fma(p, r, CR_LOG_C0);
+    double p = CR_PL(6);
+    p = fma(p, r, CR_PL(5));
+    p = fma(p, r, CR_PL(4));
+    p = fma(p, r, CR_PL(3));
+    p = fma(p, r, CR_PL(2));
+    p = fma(p, r, CR_PL(1));
+    p = fma(p, r, CR_PL(0));
     const dd lc = tab2(cr_log_logc, i);
     const double L = ((double)k + lc.hi) + fma(p, r, lc.lo);
     if (near_float_midpoint(L)) return log2f_careful<false>(x);
@@ -314,18 +314,91 @@ CR_HD float cr_exp2f(float y) {
     const float f = y - k64 * 0.015625f;               // exact, |f| <= 1/128
     const int j = k & 63, n = k >> 6;
     const double fd = (double)f;
-    double q = CR_EXP_C6;
-    q = fma(q, fd, CR_EXP_C5);
-    q = fma(q, fd, CR_EXP_C4);
-    q = fma(q, fd, CR_EXP_C3);
-    q = fma(q, fd, CR_EXP_C2);
-    q = fma(q, fd, CR_EXP_C1);
+    double q = CR_PE(6);
+    q = fma(q, fd, CR_PE(5));
+    q = fma(q, fd, CR_PE(4));
+    q = fma(q, fd, CR_PE(3));
+    q = fma(q, fd, CR_PE(2));
+    q = fma(q, fd, CR_PE(1));
     q = q * fd;
     const double T = tab(cr_exp2_tab_hi, j);
     double rr = fma(T, q, T);
     rr = u2d(d2u(rr) + ((uint64_t)(int64_t)n << 52));  // * 2^n
     if (near_float_midpoint(rr)) return exp2f_careful<false>(y);
     return (float)rr;
+}
+
+// Lockstep form for W values: out[j] = CR(2^(CR(p * CR(log2 x[j])))), the
+// Adam denominator exp2(p*log2(x)).  Evaluating the W values side by side
+// gives the scheduler independent double-precision chains, and one branch
+// per stage sends only the rare hard cases to the careful paths.
+template <int W>
+CR_HD void cr_pow2log2(const float (&x)[W], float p, float (&out)[W]) {
+    bool bad = false;
+    double r[W], acc[W], L[W];
+    int k[W];
+    dd lc[W];
+    float Lf[W];
+#pragma unroll
+    for (int j = 0; j < W; ++j) {
+        const uint32_t ix = f2u(x[j]);
+        bad |= (ix - 0x00800000u >= 0x7F000000u);
+        const uint32_t tmp = ix - CR_LOG_OFF;
+        const int i = (int)((tmp >> 16) & 127u);
+        k[j] = (int32_t)tmp >> 23;
+        const float z = u2f(ix - (tmp & 0xff800000u));
+        r[j] = fma((double)z, tab(cr_log_invc, i), -1.0);  // exact
+        lc[j] = tab2(cr_log_logc, i);
+        acc[j] = CR_PL(6);
+    }
+#pragma unroll
+    for (int c = 5; c >= 0; --c) {
+#pragma unroll
+        for (int j = 0; j < W; ++j) acc[j] = fma(acc[j], r[j], CR_PL(c));
+    }
+#pragma unroll
+    for (int j = 0; j < W; ++j) {
+        L[j] = ((double)k[j] + lc[j].hi) + fma(acc[j], r[j], lc[j].lo);
+        bad |= near_float_midpoint(L[j]);
+        Lf[j] = (float)L[j];
+    }
+    if (bad) {
+#pragma unroll
+        for (int j = 0; j < W; ++j) Lf[j] = cr_log2f<false>(x[j]);
+    }
+    // 2^y, y = p * L
+    bad = false;
+    double q[W], T[W];
+    float y[W];
+    int n[W];
+#pragma unroll
+    for (int j = 0; j < W; ++j) {
+        y[j] = p * Lf[j];
+        bad |= !(y[j] >= -126.0f && y[j] < 128.0f);
+        const float t = y[j] * 64.0f + 12582912.0f;
+        const int kk = (int)(f2u(t) - 0x4B400000u);
+        const float f = y[j] - (t - 12582912.0f) * 0.015625f;
+        n[j] = kk >> 6;
+        T[j] = tab(cr_exp2_tab_hi, kk & 63);
+        r[j] = (double)f;
+        q[j] = CR_PE(6);
+    }
+#pragma unroll
+    for (int c = 5; c >= 1; --c) {
+#pragma unroll
+        for (int j = 0; j < W; ++j) q[j] = fma(q[j], r[j], CR_PE(c));
+    }
+#pragma unroll
+    for (int j = 0; j < W; ++j) {
+        double rr = fma(T[j], q[j] * r[j], T[j]);
+        rr = u2d(d2u(rr) + ((uint64_t)(int64_t)n[j] << 52));
+        bad |= near_float_midpoint(rr);
+        out[j] = (float)rr;
+    }
+    if (bad) {
+#pragma unroll
+        for (int j = 0; j < W; ++j) out[j] = cr_exp2f<false>(y[j]);
+    }
 }
 
 }  // namespace crmath

@@ -34,37 +34,49 @@ struct ElemOut {
 // Flag sets with their own kernel instantiation; anything else runs the
 // instantiation that reads the flags at run time (FL_DYNAMIC).
 constexpr uint32_t FL_DYNAMIC = 0x80000000u;
+// set in an instantiation's flag word: wd_sv == wd_sf == 0 (checked at launch)
+constexpr uint32_t FL_ZERO_WD = 0x40000000u;
 constexpr uint32_t FL_BARE = CONCORD_F_MASS_PRESERVE | CONCORD_F_APPLY_CHASE | CONCORD_F_TRACK_REBALANCE |
-                             CONCORD_F_GF_TRUST | CONCORD_F_COHPRE | CONCORD_F_FIXED_COH;
+                             CONCORD_F_GF_TRUST | CONCORD_F_COHPRE | CONCORD_F_FIXED_COH | FL_ZERO_WD;
 constexpr uint32_t FL_NOCOHPRE = FL_BARE & ~CONCORD_F_COHPRE;
 
 template <uint32_t FL>
 __device__ __forceinline__ uint32_t flags_of(const concord_step_params& P) {
-    return (FL & FL_DYNAMIC) ? P.flags : FL;
+    return (FL & FL_DYNAMIC) ? P.flags : (FL & 0xffffu);
 }
 
-// One element of the AdamW-path step (packed_b.py:476-703).
-template <uint32_t FL>
-__device__ __forceinline__ ElemOut step_adamw(const concord_step_params& P, int32_t packed, float g,
+// First half of one AdamW-path element (packed_b.py:476-557): everything up
+// to the argument x = v_proxy + eps of the denominator exp2(p*log2(x)).
+struct AdamwPre {
+    int32_t s_fast, s_slow, v_slow, te;
+    float g, d_fs, coh, cp, x;
+    float coh_num, coh_den;  // fixed gate: coh = coh_num / coh_den (divided later)
+};
+
+// 2^te; SAFE promises |te| <= 126, so the bits can be written directly
+template <bool SAFE>
+__device__ __forceinline__ float pow2_exp(int32_t te) {
+    return SAFE ? __uint_as_float((uint32_t)(te + 127) << 23) : exp2i(te);
+}
+
+template <uint32_t FL, bool SAFE = false>
+__device__ __forceinline__ AdamwPre adamw_pre(const concord_step_params& P, int32_t packed, float g,
                                               int32_t row_e, int32_t col_e, float v_row, float v_col,
-                                              float cp, const StepScalars& S, int32_t pos) {
+                                              float cp, const StepScalars& S) {
     const uint32_t F = flags_of<FL>(P);
-    int32_t s_fast = packed >> 16;
-    int32_t s_slow = shl32(packed, 16) >> 24;
-    int32_t v_slow = shl32(packed, 24) >> 24;
-    int32_t s_slow_full = s_slow * 128;
-    int32_t v_slow_full = v_slow * 128;
-
-    int32_t te = row_e + col_e - P.mantissa_bias;
-    float scale_fwd = exp2i(te);
-    float scale_inv = exp2i(-te);
-
-    float d_fs = (float)s_fast;
-    float d_sv = (float)(s_slow_full - v_slow_full);
-    float noise = d_fs - P.drift_cancel_C * d_sv;
-    float noise_in_w = noise * scale_fwd;
+    AdamwPre e;
+    e.s_fast = packed >> 16;
+    e.s_slow = shl32(packed, 16) >> 24;
+    e.v_slow = shl32(packed, 24) >> 24;
+    e.te = row_e + col_e - P.mantissa_bias;
+    e.g = g;
+    e.cp = cp;
+    const float scale_fwd = pow2_exp<SAFE>(e.te);
+    e.d_fs = (float)e.s_fast;
+    const float d_sv = (float)(e.s_slow * 128 - e.v_slow * 128);
+    const float noise = e.d_fs - P.drift_cancel_C * d_sv;
+    const float noise_in_w = noise * scale_fwd;
     float v_proxy = noise_in_w * noise_in_w * P.v_scale;
-
     const bool need_vhat = (F & (CONCORD_F_GF_TRUST | CONCORD_F_GF_CONSOL | CONCORD_F_COHPRE | CONCORD_F_RATIO_COH)) != 0;
     const bool need_coh = (F & (CONCORD_F_GF_CONSOL | CONCORD_F_COHPRE | CONCORD_F_RATIO_COH)) != 0;
     float v_hat = 0.0f, coh = 0.0f;
@@ -72,22 +84,42 @@ __device__ __forceinline__ ElemOut step_adamw(const concord_step_params& P, int3
     if (F & CONCORD_F_GF_TRUST) v_proxy = v_proxy + P.gf_trust_delta_sq * v_hat;
     if (need_coh) {
         if (F & CONCORD_F_FIXED_COH) {
-            float sig_w = P.drift_cancel_C * d_sv * scale_fwd;
-            float sig2 = sig_w * sig_w;
-            coh = sig2 / (sig2 + noise_in_w * noise_in_w + 1e-30f);
+            const float sig_w = P.drift_cancel_C * d_sv * scale_fwd;
+            const float sig2 = sig_w * sig_w;
+            // 0 <= sig2 <= den: the reference's clamp is the identity (NaN propagates)
+            e.coh_num = sig2;
+            e.coh_den = sig2 + noise_in_w * noise_in_w + 1e-30f;
+            coh = 0.0f;  // = coh_num / coh_den, see fixed_coh_divide
         } else {
-            float mg = P.alpha_v_fast * d_sv * scale_fwd;
-            coh = mg * mg / (v_hat + 1e-12f);
+            const float mg = P.alpha_v_fast * d_sv * scale_fwd;
+            coh = np_min(np_max(mg * mg / (v_hat + 1e-12f), 0.0f), 1.0f);
         }
-        // with the fixed gate 0 <= sig2 <= den, so the clamp is the identity
-        // (a NaN propagates either way)
-        if (!(F & CONCORD_F_FIXED_COH)) coh = np_min(np_max(coh, 0.0f), 1.0f);
     }
+    e.coh = coh;
+    e.x = v_proxy + S.eps;
+    return e;
+}
 
-    float denom_p = crmath::cr_exp2f(P.precond_p * crmath::cr_log2f(v_proxy + S.eps));
-    float step_live = g / denom_p;
-    step_live = clamp_np(step_live, P.step_cap);
+// the fixed-gate division of adamw_pre, done separately so that the four
+// divisions of a thread sit next to each other
+template <uint32_t FL>
+__device__ __forceinline__ void fixed_coh_divide(const concord_step_params& P, AdamwPre& e) {
+    const uint32_t F = flags_of<FL>(P);
+    if ((F & (CONCORD_F_GF_CONSOL | CONCORD_F_COHPRE | CONCORD_F_RATIO_COH)) && (F & CONCORD_F_FIXED_COH))
+        e.coh = e.coh_num / e.coh_den;
+}
 
+// Second half (packed_b.py:558-703), given denom_p = exp2(p*log2(x)).
+template <uint32_t FL, bool SAFE = false>
+__device__ __forceinline__ ElemOut adamw_post(const concord_step_params& P, const AdamwPre& e,
+                                              float step_div, const StepScalars& S, int32_t pos) {
+    const uint32_t F = flags_of<FL>(P);
+    const float scale_fwd = pow2_exp<SAFE>(e.te);
+    const float scale_inv = pow2_exp<SAFE>(-e.te);
+    const float coh = e.coh, d_fs = e.d_fs;
+    int32_t s_fast = e.s_fast, s_slow = e.s_slow;
+    const int32_t v_slow = e.v_slow;
+    float step_live = clamp_np(step_div, P.step_cap);  // step_div = g / denom_p
     const bool consol = (F & CONCORD_F_GF_CONSOL) != 0;
     float evap = 0.0f;
     if (consol) {
@@ -101,44 +133,45 @@ __device__ __forceinline__ ElemOut step_adamw(const concord_step_params& P, int3
     s_fast = s_fast + sr_tick(delta_t, hash_uniform(s_fast, pos, S.salt));
 
     int32_t new_v = v_slow;
-    float cp_new = cp;
+    float cp_new = e.cp;
     if (F & CONCORD_F_APPLY_CHASE) {
         float chase_mantissa;
         if (F & CONCORD_F_RATIO_COH) {
-            float gate = P.chase_floor + P.one_minus_chase_floor * coh;
+            const float gate = P.chase_floor + P.one_minus_chase_floor * coh;
             chase_mantissa = P.alpha * gate * P.gate_gain * (float)s_fast;
         } else if (F & CONCORD_F_COHPRE) {
-            float gate = coh + cp * (1.0f - coh);
-            cp_new = P.one_minus_alpha_v_fast * cp + P.alpha_v_fast * coh;
+            const float gate = coh + e.cp * (1.0f - coh);
+            cp_new = P.one_minus_alpha_v_fast * e.cp + P.alpha_v_fast * coh;
             chase_mantissa = P.alpha * gate * P.gate_gain * (float)s_fast;
         } else {
             chase_mantissa = P.alpha_gate_gain * (float)s_fast;
         }
-        int32_t ts = sr_tick(chase_mantissa / 128.0f, hash_uniform(s_fast, pos, S.salt ^ 0x5A5A5A5A));
+        const int32_t ts = sr_tick(chase_mantissa / 128.0f, hash_uniform(s_fast, pos, S.salt ^ 0x5A5A5A5A));
         s_slow = s_slow + ts;
         s_fast = s_fast - ts * 128;
 
-        float delta_v8 = P.alpha_v_fast * (float)(s_slow * 128 - v_slow_full) / 128.0f;
+        float delta_v8 = P.alpha_v_fast * (float)(s_slow * 128 - v_slow * 128) / 128.0f;
         if (F & CONCORD_F_RATIO_COH)
             delta_v8 = delta_v8 * (P.leak_floor + P.one_minus_leak_floor * coh);
-        int32_t tv = sr_tick(delta_v8, hash_uniform(s_fast, pos, S.salt ^ 0x33335555));
+        const int32_t tv = sr_tick(delta_v8, hash_uniform(s_fast, pos, S.salt ^ 0x33335555));
         new_v = clampi(v_slow + tv, -128, 127);
         if (F & CONCORD_F_MASS_PRESERVE) s_slow = s_slow - (new_v - v_slow);
 
-        int32_t v_full_post = new_v * 128;
-        if (P.wd_sv != 0.0f) {  // a zero rate gives tick 0 for every finite state
-            float d = S.lr * P.wd_sv * (float)(s_slow * 128 - v_full_post) / 128.0f;
+        const int32_t v_full_post = new_v * 128;
+        const bool zero_wd = (FL & FL_ZERO_WD) != 0;
+        if (!zero_wd && P.wd_sv != 0.0f) {  // a zero rate gives tick 0 for every finite state
+            const float d = S.lr * P.wd_sv * (float)(s_slow * 128 - v_full_post) / 128.0f;
             s_slow = s_slow - sr_tick(d, hash_uniform(s_fast, pos, S.salt ^ 0x66665555));
         }
-        if (P.wd_sf != 0.0f) {
-            float d = S.lr * P.wd_sf * (float)(s_slow * 128 + s_fast - v_full_post);
+        if (!zero_wd && P.wd_sf != 0.0f) {
+            const float d = S.lr * P.wd_sf * (float)(s_slow * 128 + s_fast - v_full_post);
             s_fast = s_fast - sr_tick(d, hash_uniform(s_fast, pos, S.salt ^ 0x77770000));
         }
     }
 
-    int32_t sfc = clampi(s_fast, -32768, 32767);
-    int32_t ssc = clampi(s_slow, -128, 127);
-    int32_t m_new = ssc * 128 + sfc + new_v * 128;
+    const int32_t sfc = clampi(s_fast, -32768, 32767);
+    const int32_t ssc = clampi(s_slow, -128, 127);
+    const int32_t m_new = ssc * 128 + sfc + new_v * 128;
     ElemOut o;
     o.word = repack(sfc, ssc, new_v);
     o.wval = (float)m_new * scale_fwd;
@@ -146,6 +179,26 @@ __device__ __forceinline__ ElemOut step_adamw(const concord_step_params& P, int3
     o.coh = coh;
     o.coh_pre = cp_new;
     return o;
+}
+
+// One element of the AdamW-path step (packed_b.py:476-703).
+template <uint32_t FL>
+__device__ __forceinline__ ElemOut step_adamw(const concord_step_params& P, int32_t packed, float g,
+                                              int32_t row_e, int32_t col_e, float v_row, float v_col,
+                                              float cp, const StepScalars& S, int32_t pos) {
+    AdamwPre e = adamw_pre<FL>(P, packed, g, row_e, col_e, v_row, v_col, cp, S);
+    fixed_coh_divide<FL>(P, e);
+    const float denom_p = crmath::cr_exp2f(P.precond_p * crmath::cr_log2f(e.x));
+    return adamw_post<FL>(P, e, e.g / denom_p, S, pos);
+}
+
+// Out-of-line element for rows/columns whose exponents could leave the
+// normal fp32 range (never the case for exponents in [EXP_MIN, EXP_MAX]).
+template <uint32_t FL>
+__device__ __noinline__ ElemOut step_adamw_outlined(const concord_step_params& P, int32_t packed, float g,
+                                                   int32_t row_e, int32_t col_e, float v_row, float v_col,
+                                                   float cp, const StepScalars& S, int32_t pos) {
+    return step_adamw<FL>(P, packed, g, row_e, col_e, v_row, v_col, cp, S, pos);
 }
 
 // One element of the SGD-path step (packed_b.py:214-312).
@@ -269,37 +322,88 @@ __global__ void __launch_bounds__(STEP_THREADS, MINB) step_vec_kernel(StepArgs A
 #pragma unroll
         for (int j = 0; j < VEC; ++j) ce[j] = (int32_t)(int8_t)(c4 >> (8 * j));
         if (need_vhat) {
-            float4 a = __ldg(reinterpret_cast<const float4*>(A.v_col + k0));
+            const float4 a = __ldg(reinterpret_cast<const float4*>(A.v_col + k0));
             vc[0] = a.x; vc[1] = a.y; vc[2] = a.z; vc[3] = a.w;
         }
     }
+    bool cols_safe = true;
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) cols_safe &= (uint32_t)(ce[j] + 63) <= 126u;
     float csum = 0.0f;
     int ccnt = 0;
+    // rows of this warp: rbase + warp + 8 i; the next row's inputs are loaded
+    // before the current row is computed (registers as a 2-stage pipeline)
+    int4 nw4 = make_int4(0, 0, 0, 0);
+    uint2 ng4 = make_uint2(0, 0);
+    float4 ncp = make_float4(1.0f, 1.0f, 1.0f, 1.0f);
+    int32_t nre = 0;
+    float nvr = 0.0f;
+    auto prefetch = [&](int64_t n) {
+        if (n < A.N && active) {
+            nre = A.row_exp[n];
+            nvr = need_vhat ? __ldg(A.v_row + n) : 0.0f;
+            nw4 = __ldcs(reinterpret_cast<const int4*>(A.packed + n * A.ldp + k0));
+            ng4 = __ldcs(reinterpret_cast<const uint2*>(A.grad + n * A.ldg + k0));
+            if (use_cp) ncp = __ldcs(reinterpret_cast<const float4*>(A.coh_pre + n * A.ldc + k0));
+        }
+    };
+    prefetch(rbase + warp);
     for (int r = warp; r < STEP_ROWS; r += STEP_THREADS / 32) {
         const int64_t n = rbase + r;
         if (n >= A.N) break;
         int rml = 0;
+        const int4 w4 = nw4;
+        const uint2 g4 = ng4;
+        const float4 cpv = ncp;
+        const int32_t re = nre;
+        const float vr = nvr;
+        if (r + STEP_THREADS / 32 < STEP_ROWS) prefetch(n + STEP_THREADS / 32);
         if (active) {
-            const int32_t re = A.row_exp[n];
-            const float vr = need_vhat ? __ldg(A.v_row + n) : 0.0f;
             int32_t* pw = A.packed + n * A.ldp + k0;
-            int4 w4 = __ldcs(reinterpret_cast<const int4*>(pw));
-            uint2 g4 = __ldcs(reinterpret_cast<const uint2*>(A.grad + n * A.ldg + k0));
-            float cp[VEC] = {1.0f, 1.0f, 1.0f, 1.0f};
+            float cp[VEC] = {cpv.x, cpv.y, cpv.z, cpv.w};
             float* pc = use_cp ? A.coh_pre + n * A.ldc + k0 : nullptr;
-            if (use_cp) {
-                float4 a = __ldcs(reinterpret_cast<const float4*>(pc));
-                cp[0] = a.x; cp[1] = a.y; cp[2] = a.z; cp[3] = a.w;
-            }
             int32_t wv[VEC] = {w4.x, w4.y, w4.z, w4.w};
             const uint32_t gw[2] = {g4.x, g4.y};
             float wf[VEC];
             const int32_t posn = shl32((int32_t)(A.row0 + n), 16);
+            ElemOut outs[VEC];
+            const bool safe = cols_safe && (uint32_t)(re - A.P.mantissa_bias + 63) <= 126u;
+            if (KIND == CONCORD_KIND_ADAMW && !safe) {
+#pragma unroll
+                for (int j = 0; j < VEC; ++j) {
+                    const float g = bf16_to_f32((gw[j >> 1] >> ((j & 1) * 16)) & 0xffffu);
+                    outs[j] = step_adamw_outlined<FL>(A.P, wv[j], g, re, ce[j], vr, vc[j], cp[j], S,
+                                                      posn ^ (int32_t)(k0 + j));
+                }
+            } else if (KIND == CONCORD_KIND_ADAMW) {
+                // phase 1: up to the denominator's argument; phase 2: the four
+                // correctly rounded exp2(p*log2(x)) side by side; phase 3: the rest
+                AdamwPre pre[VEC];
+                float xs[VEC], den[VEC];
+#pragma unroll
+                for (int j = 0; j < VEC; ++j) {
+                    const float g = bf16_to_f32((gw[j >> 1] >> ((j & 1) * 16)) & 0xffffu);
+                    pre[j] = adamw_pre<FL, true>(A.P, wv[j], g, re, ce[j], vr, vc[j], cp[j], S);
+                    xs[j] = pre[j].x;
+                }
+#pragma unroll
+                for (int j = 0; j < VEC; ++j) fixed_coh_divide<FL>(A.P, pre[j]);
+                crmath::cr_pow2log2<VEC>(xs, A.P.precond_p, den);
+#pragma unroll
+                for (int j = 0; j < VEC; ++j) den[j] = pre[j].g / den[j];
+#pragma unroll
+                for (int j = 0; j < VEC; ++j)
+                    outs[j] = adamw_post<FL, true>(A.P, pre[j], den[j], S, posn ^ (int32_t)(k0 + j));
+            } else {
+#pragma unroll
+                for (int j = 0; j < VEC; ++j) {
+                    const float g = bf16_to_f32((gw[j >> 1] >> ((j & 1) * 16)) & 0xffffu);
+                    outs[j] = step_sgd<FL>(A.P, wv[j], g, re, ce[j], S, posn ^ (int32_t)(k0 + j));
+                }
+            }
 #pragma unroll
             for (int j = 0; j < VEC; ++j) {
-                const float g = bf16_to_f32((gw[j >> 1] >> ((j & 1) * 16)) & 0xffffu);
-                const int32_t pos = posn ^ (int32_t)(k0 + j);
-                ElemOut o = step_elem<KIND, FL>(A.P, wv[j], g, re, ce[j], vr, vc[j], cp[j], S, pos);
+                const ElemOut& o = outs[j];
                 wv[j] = o.word;
                 cp[j] = o.coh_pre;
                 wf[j] = o.wval;
@@ -372,9 +476,10 @@ __global__ void __launch_bounds__(STEP_THREADS) step_generic_kernel(StepArgs A) 
 
 template <int MINB>
 static void launch_vec(bool adamw, uint32_t F, bool has_cp, dim3 grid, cudaStream_t s, const StepArgs& A) {
+    const bool zero_wd = A.P.wd_sv == 0.0f && A.P.wd_sf == 0.0f;
     if (!adamw) step_vec_kernel<CONCORD_KIND_SGD, FL_DYNAMIC, MINB><<<grid, STEP_THREADS, 0, s>>>(A);
-    else if (F == FL_BARE && has_cp) step_vec_kernel<CONCORD_KIND_ADAMW, FL_BARE, MINB><<<grid, STEP_THREADS, 0, s>>>(A);
-    else if (F == FL_NOCOHPRE) step_vec_kernel<CONCORD_KIND_ADAMW, FL_NOCOHPRE, MINB><<<grid, STEP_THREADS, 0, s>>>(A);
+    else if (F == (FL_BARE & 0xffffu) && has_cp && zero_wd) step_vec_kernel<CONCORD_KIND_ADAMW, FL_BARE, MINB><<<grid, STEP_THREADS, 0, s>>>(A);
+    else if (F == (FL_NOCOHPRE & 0xffffu) && zero_wd) step_vec_kernel<CONCORD_KIND_ADAMW, FL_NOCOHPRE, MINB><<<grid, STEP_THREADS, 0, s>>>(A);
     else step_vec_kernel<CONCORD_KIND_ADAMW, FL_DYNAMIC, MINB><<<grid, STEP_THREADS, 0, s>>>(A);
 }
 
@@ -417,10 +522,10 @@ extern "C" int concord_step(const concord_step_params* p, int32_t* packed, int64
     if (vec) {
         dim3 grid((unsigned)((K + STEP_COLS - 1) / STEP_COLS), (unsigned)((N + STEP_ROWS - 1) / STEP_ROWS));
         if (grid.y > 65535) return fail(CONCORD_ETOOBIG, "concord_step: too many rows for one launch");
-        // resident blocks per SM the register budget is tuned for (CONCORD_STEP_MINB=2|3)
+        // resident blocks per SM the register budget targets (default 2; CONCORD_STEP_MINB=3)
         static const int minb = [] {
             const char* e = getenv("CONCORD_STEP_MINB");
-            return (e && e[0] == '2') ? 2 : 3;
+            return (e && e[0] == '3') ? 3 : 2;
         }();
         if (minb == 2) launch_vec<2>(adamw, F, coh_pre != nullptr, grid, s, A);
         else launch_vec<3>(adamw, F, coh_pre != nullptr, grid, s, A);
