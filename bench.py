@@ -130,18 +130,30 @@ def make_grads(n_rows, k_cols, device, count=2, seed=1):
     return grads, gemm_ms
 
 
+SHARDED = None
+
+
 def optimizer_step(layer, grad, coh_stats=None, ev=None):
-    """The timed unit: v-hat + fused packed step + rebalance of one layer."""
+    """The timed unit: v-hat + fused packed step + rebalance of one layer
+    (on N > 1 GPUs: the row-sharded data-parallel step, collectives included)."""
     if ev is not None:
         ev[0].record()
-    layer.optimizer_step(grad, coh_stats=coh_stats, step_events=ev)
+    if SHARDED is not None:
+        SHARDED.step_events = ev
+        SHARDED.step(grad)
+    else:
+        layer.optimizer_step(grad, coh_stats=coh_stats, step_events=ev)
     layer.rebalance()
 
 
 def bench_ours(args, rank, world, device):
+    global SHARDED
     n_rows, k_cols = args.rows, args.cols
     layer = setup_layer(n_rows, k_cols, device)
-    grads, gemm_ms = make_grads(n_rows, k_cols, device)
+    grads, gemm_ms = make_grads(n_rows, k_cols, device, seed=1 + rank)
+    if world > 1:
+        from concord_b200.distributed import RowShardedStep
+        SHARDED = RowShardedStep(layer)
     params = n_rows * k_cols
     bytes_step = params * (STEP_BYTES_PER_PARAM + VHAT_BYTES_PER_PARAM)
     for i in range(args.warmup):
@@ -247,13 +259,14 @@ def emit(d):
 def base_line(args, world):
     return {"metric": "fused bwd+packed-step HBM GB/s", "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int32 words / fp32 math / bf16 grad",
+            "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "int32 words / fp32 math / bf16 grad",
             "data": "synthetic: W0~N(0,0.02) quantized, dW = dY^T X / M with X,dY ~ N(0,1) bf16",
             "config": {"workload": f"C2 dequant-matmul + packed-step sweep, largest shape "
                                    f"(M={M}, K={args.cols}, N={args.rows}); bare-default ConcordLinearPackedB",
                        "M": M, "K": args.cols, "N": args.rows, "params": args.rows * args.cols,
                        "l2_flush": "not needed: working set > 126 MB L2",
-                       "parallelism": f"replicas x{world}" if world > 1 else "single"}}
+                       "parallelism": (f"dp{world}: row-sharded packed step (NCCL reduce-scatter bf16 dW, "
+                                       "all-gather int32 words)") if world > 1 else "single"}}
 
 
 def main():
@@ -299,20 +312,22 @@ def main():
     packed_b._lib()
     r = bench_ours(args, rank, world, device)
     hbm, tf, src = peaks()
-    value = r["bytes_step"] * world / (r["ms"] * 1e-3) / 1e9
-    achieved = r["params"] * STEP_BYTES_PER_PARAM / (r["step_kernel_ms"] * 1e-3) / 1e9
+    # one layer update per step whatever the GPU count (the update is sharded)
+    value = r["bytes_step"] / (r["ms"] * 1e-3) / 1e9
+    shard_params = r["params"] if world == 1 else SHARDED.S * args.cols
+    achieved = shard_params * STEP_BYTES_PER_PARAM / (r["step_kernel_ms"] * 1e-3) / 1e9
     if rank != 0:
         return
     d = base_line(args, world)
     flops = 2.0 * M * args.rows * args.cols
     d.update({
         "value": value, "ms_per_step": r["ms"],
-        "e2e": {"value": r["bytes_step"] * world / (r["e2e_ms"] * 1e-3) / 1e9, "unit": "GB/s",
+        "e2e": {"value": r["bytes_step"] / (r["e2e_ms"] * 1e-3) / 1e9, "unit": "GB/s",
                 "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "traffic": None, "peak_source": src,
                      "kernel": "concord_step (step_vec_kernel<adamw>)",
-                     "algorithmic_bytes_per_launch": r["params"] * STEP_BYTES_PER_PARAM,
+                     "algorithmic_bytes_per_launch": shard_params * STEP_BYTES_PER_PARAM,
                      "kernel_ms": r["step_kernel_ms"]},
         "vhat_ms": r["vhat_ms"],
         "gemm": {k: {"ms": v, "tflops": flops / (v * 1e-3) / 1e12} for k, v in r["gemm_ms"].items()},

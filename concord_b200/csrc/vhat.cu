@@ -36,6 +36,8 @@ struct VhatArgs {
     unsigned* cnt;    // [nrb] row-block arrivals, [ncs] slab arrivals, [1] global
     int ncs, nrb;
     bool vec;
+    float* col_sum_out;  // shard mode: raw column sums of g^2 (v_col untouched)
+    float* vsum_out;     // shard mode: sum of this shard's updated v_row
 };
 
 __global__ void __launch_bounds__(VH_THREADS) vhat_kernel(VhatArgs A) {
@@ -120,7 +122,8 @@ __global__ void __launch_bounds__(VH_THREADS) vhat_kernel(VhatArgs A) {
         if (col < A.K) {
             float t = __ldcg(A.cp + col);
             for (int b = 1; b < A.nrb; ++b) t = t + __ldcg(A.cp + (int64_t)b * A.K + col);
-            A.v_col[col] = A.b2 * A.v_col[col] + A.omb2 * t;
+            if (A.col_sum_out) A.col_sum_out[col] = t;
+            else A.v_col[col] = A.b2 * A.v_col[col] + A.omb2 * t;
         }
         if (threadIdx.x == 0) cnt_cs[cs] = 0;
     }
@@ -152,12 +155,24 @@ __global__ void __launch_bounds__(VH_THREADS) vhat_kernel(VhatArgs A) {
                 __syncthreads();
             }
             if (threadIdx.x == 0) {
-                float sv = np_max(red[0], 1e-30f);
-                *A.sum_v_inv = 1.0f / sv;
+                if (A.vsum_out) {
+                    *A.vsum_out = red[0];
+                } else {
+                    float sv = np_max(red[0], 1e-30f);
+                    *A.sum_v_inv = 1.0f / sv;
+                }
                 *cnt_g = 0;
             }
         }
     }
+}
+
+// shard mode, after the all-reduce of (column sums, v_row sum) over ranks
+__global__ void vhat_finish_kernel(const float* col_sum, const float* vsum, float* v_col, float* sum_v_inv,
+                                   int64_t K, float b2, float omb2) {
+    for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < K; k += (int64_t)gridDim.x * blockDim.x)
+        v_col[k] = b2 * v_col[k] + omb2 * col_sum[k];
+    if (blockIdx.x == 0 && threadIdx.x == 0) *sum_v_inv = 1.0f / np_max(*vsum, 1e-30f);
 }
 
 }  // namespace concord
@@ -182,24 +197,51 @@ extern "C" size_t concord_vhat_workspace_bytes(int64_t N, int64_t K) {
     return t;
 }
 
+static int vhat_launch(const uint16_t* grad, int64_t ldg, int64_t N, int64_t K, float* v_row, float* v_col,
+                       float* sum_v_inv, float beta2, float one_minus_beta2, int32_t* row_max, int32_t* col_max,
+                       int32_t* salt, float* col_sum_out, float* vsum_out, void* workspace,
+                       size_t workspace_bytes, void* stream, const char* name) {
+    if (N <= 0 || K <= 0 || ldg < K) return fail(CONCORD_ESHAPE, std::string(name) + ": bad shape/stride");
+    int ncs, nrb; size_t off_rp, off_cp, total;
+    vhat_layout(N, K, &ncs, &nrb, &off_rp, &off_cp, &total);
+    if (!workspace || workspace_bytes < total)
+        return fail(CONCORD_EWORKSPACE, std::string(name) + ": workspace smaller than concord_vhat_workspace_bytes(N, K)");
+    if (nrb > 65535) return fail(CONCORD_ETOOBIG, std::string(name) + ": too many rows for one launch");
+    char* ws = static_cast<char*>(workspace);
+    VhatArgs A{grad, ldg, N, K, v_row, v_col, sum_v_inv, beta2, one_minus_beta2, row_max, col_max, salt,
+               reinterpret_cast<float*>(ws + off_rp), reinterpret_cast<float*>(ws + off_cp),
+               reinterpret_cast<unsigned*>(ws), ncs, nrb,
+               (K % 8 == 0) && (ldg % 8 == 0) && aligned(grad, 16), col_sum_out, vsum_out};
+    dim3 grid((unsigned)ncs, (unsigned)nrb);
+    vhat_kernel<<<grid, VH_THREADS, 0, as_stream(stream)>>>(A);
+    return check_launch(name);
+}
+
 extern "C" int concord_vhat_update(const uint16_t* grad, int64_t ldg, int64_t N, int64_t K,
                                    float* v_row, float* v_col, float* sum_v_inv, float beta2,
                                    float one_minus_beta2, int32_t* row_max, int32_t* col_max,
                                    int32_t* salt, void* workspace, size_t workspace_bytes,
                                    void* stream) {
     if (!grad || !v_row || !v_col || !sum_v_inv) return fail(CONCORD_EINVAL, "concord_vhat_update: null pointer");
-    if (N <= 0 || K <= 0 || ldg < K) return fail(CONCORD_ESHAPE, "concord_vhat_update: bad shape/stride");
-    int ncs, nrb; size_t off_rp, off_cp, total;
-    vhat_layout(N, K, &ncs, &nrb, &off_rp, &off_cp, &total);
-    if (!workspace || workspace_bytes < total)
-        return fail(CONCORD_EWORKSPACE, "concord_vhat_update: workspace smaller than concord_vhat_workspace_bytes(N, K)");
-    if (nrb > 65535) return fail(CONCORD_ETOOBIG, "concord_vhat_update: too many rows for one launch");
-    char* ws = static_cast<char*>(workspace);
-    VhatArgs A{grad, ldg, N, K, v_row, v_col, sum_v_inv, beta2, one_minus_beta2, row_max, col_max, salt,
-               reinterpret_cast<float*>(ws + off_rp), reinterpret_cast<float*>(ws + off_cp),
-               reinterpret_cast<unsigned*>(ws), ncs, nrb,
-               (K % 8 == 0) && (ldg % 8 == 0) && aligned(grad, 16)};
-    dim3 grid((unsigned)ncs, (unsigned)nrb);
-    vhat_kernel<<<grid, VH_THREADS, 0, as_stream(stream)>>>(A);
-    return check_launch("concord_vhat_update");
+    return vhat_launch(grad, ldg, N, K, v_row, v_col, sum_v_inv, beta2, one_minus_beta2, row_max, col_max, salt,
+                       nullptr, nullptr, workspace, workspace_bytes, stream, "concord_vhat_update");
+}
+
+extern "C" int concord_vhat_partial(const uint16_t* grad, int64_t ldg, int64_t N, int64_t K, float* v_row,
+                                    float beta2, float one_minus_beta2, int32_t* row_max, int32_t* col_max,
+                                    int32_t* salt, float* col_sum_out, float* vsum_out, void* workspace,
+                                    size_t workspace_bytes, void* stream) {
+    if (!grad || !v_row || !col_sum_out || !vsum_out) return fail(CONCORD_EINVAL, "concord_vhat_partial: null pointer");
+    return vhat_launch(grad, ldg, N, K, v_row, nullptr, nullptr, beta2, one_minus_beta2, row_max, col_max, salt,
+                       col_sum_out, vsum_out, workspace, workspace_bytes, stream, "concord_vhat_partial");
+}
+
+extern "C" int concord_vhat_finish(const float* col_sum, const float* vsum, float* v_col, float* sum_v_inv,
+                                   int64_t K, float beta2, float one_minus_beta2, void* stream) {
+    if (!col_sum || !vsum || !v_col || !sum_v_inv) return fail(CONCORD_EINVAL, "concord_vhat_finish: null pointer");
+    if (K <= 0) return fail(CONCORD_ESHAPE, "concord_vhat_finish: bad shape");
+    int blocks = (int)((K + 255) / 256);
+    if (blocks > 1024) blocks = 1024;
+    vhat_finish_kernel<<<blocks, 256, 0, as_stream(stream)>>>(col_sum, vsum, v_col, sum_v_inv, K, beta2, one_minus_beta2);
+    return check_launch("concord_vhat_finish");
 }

@@ -129,6 +129,23 @@ int concord_vhat_update(const uint16_t* grad, int64_t ldg, int64_t N, int64_t K,
                         void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Row-sharded form of concord_vhat_update for data-parallel training
+ * (the reference has no multi-GPU code; this splits its v-hat update,
+ * packed_b.py:1288-1303, at the one point that needs all rows).  On this
+ * rank's shard grad [N,K]: v_row is updated in place; col_sum_out[K]
+ * receives the shard's column sums of g^2 and *vsum_out the sum of the
+ * shard's updated v_row.  The caller all-reduces (col_sum_out, vsum_out)
+ * over ranks, then concord_vhat_finish applies v_col = b2*v_col +
+ * (1-b2)*col_sum and sum_v_inv = 1/max(vsum, 1e-30).
+ */
+int concord_vhat_partial(const uint16_t* grad, int64_t ldg, int64_t N, int64_t K, float* v_row,
+                         float beta2, float one_minus_beta2, int32_t* row_max, int32_t* col_max,
+                         int32_t* salt, float* col_sum_out, float* vsum_out,
+                         void* workspace, size_t workspace_bytes, void* stream);
+int concord_vhat_finish(const float* col_sum, const float* vsum, float* v_col, float* sum_v_inv,
+                        int64_t K, float beta2, float one_minus_beta2, void* stream);
+
+/*
  * One packed optimizer step over rows [0,N) of a (row-)shard whose first
  * row is global row `row0` (0 when unsharded).  Mutates packed (and
  * coh_pre when CONCORD_F_COHPRE) in place, writes the new bf16 weight to

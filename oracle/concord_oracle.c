@@ -327,8 +327,19 @@ void oracle_step(const concord_step_params* P, int32_t* packed, int64_t ldp,
  */
 #define VH_COLS 256
 #define VH_ROWS 128
+/* shard mode (concord_vhat_partial): when col_sum_out is non-NULL, the raw
+ * column totals go there (v_col untouched) and the v_row sum to *vsum_out
+ * (sum_v_inv untouched). */
+void oracle_vhat_ex(const uint16_t* grad, int64_t ldg, int64_t N, int64_t K,
+                    float* v_row, float* v_col, float* sum_v_inv, float b2, float omb2,
+                    float* col_sum_out, float* vsum_out);
 void oracle_vhat(const uint16_t* grad, int64_t ldg, int64_t N, int64_t K,
                  float* v_row, float* v_col, float* sum_v_inv, float b2, float omb2) {
+    oracle_vhat_ex(grad, ldg, N, K, v_row, v_col, sum_v_inv, b2, omb2, NULL, NULL);
+}
+void oracle_vhat_ex(const uint16_t* grad, int64_t ldg, int64_t N, int64_t K,
+                    float* v_row, float* v_col, float* sum_v_inv, float b2, float omb2,
+                    float* col_sum_out, float* vsum_out) {
     int64_t ncs = (K + VH_COLS - 1) / VH_COLS, nrb = (N + VH_ROWS - 1) / VH_ROWS;
     float* rp = (float*)calloc((size_t)(ncs * N + 1), sizeof(float));
     float* cp = (float*)calloc((size_t)(nrb * K + 1), sizeof(float));
@@ -377,7 +388,8 @@ void oracle_vhat(const uint16_t* grad, int64_t ldg, int64_t N, int64_t K,
     for (int64_t k = 0; k < K; ++k) {
         float t = cp[k];
         for (int64_t b = 1; b < nrb; ++b) t = t + cp[b * K + k];
-        v_col[k] = b2 * v_col[k] + omb2 * t;
+        if (col_sum_out) col_sum_out[k] = t;
+        else v_col[k] = b2 * v_col[k] + omb2 * t;
     }
     float a[256];
     for (int t = 0; t < 256; ++t) {
@@ -388,6 +400,7 @@ void oracle_vhat(const uint16_t* grad, int64_t ldg, int64_t N, int64_t K,
     for (int s = 128; s >= 1; s >>= 1)
         for (int t = 0; t < s; ++t) a[t] = a[t] + a[t + s];
     float sv = a[0];
+    if (vsum_out) { *vsum_out = sv; free(rp); free(cp); return; }
     sv = np_max(sv, 1e-30f);
     *sum_v_inv = 1.0f / sv;
     free(rp); free(cp);

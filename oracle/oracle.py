@@ -71,6 +71,17 @@ def vhat(grad_bf16, v_row, v_col, sum_v_inv, beta2=0.999):
                       ctypes.c_float(1.0 - beta2))
 
 
+def vhat_partial(grad_bf16, v_row, beta2=0.999):
+    """Shard form: updates v_row; returns (column sums of g^2, sum of v_row)."""
+    N, K = grad_bf16.shape
+    col_sum = np.zeros(K, np.float32)
+    vsum = np.zeros(1, np.float32)
+    lib().oracle_vhat_ex(_p(_c(grad_bf16, np.uint16)), _I64(K), _I64(N), _I64(K),
+                         _p(_c(v_row, np.float32)), None, None, ctypes.c_float(beta2),
+                         ctypes.c_float(1.0 - beta2), _p(col_sum), _p(vsum))
+    return col_sum, vsum
+
+
 def rebalance(packed, row_exp, col_exp, row_max, col_max, row_hwm, col_hwm, seed,
               max_m=24000, exp_max=7, exp_min=-8, allow_tickdown=False, row0=0,
               n_total=None):
