@@ -32,8 +32,9 @@ struct RebArgs {
     int32_t max_m, exp_max, exp_min, allow_td;
     int64_t N, K, row0, N_total;
     int32_t* fired_out;
-    int8_t* rt; int8_t* ct; int32_t* fired;
+    int8_t* rt; int8_t* ct; int32_t* fired;   // fired[0] flag, [1] #rows, [2] #cols ticked
     int32_t* rhist; int32_t* chist;
+    int32_t* rowlist; int32_t* collist;       // rows / columns whose exponent moved
 };
 
 __global__ void reb_hist_kernel(RebArgs A) {
@@ -79,7 +80,11 @@ __global__ void reb_decide_kernel(RebArgs A) {
         }
         const int t = up - dn;
         A.rt[n] = (int8_t)t;
-        if (t) { A.row_exp[n] = (int8_t)(e + t); atomicOr(A.fired, 1); }
+        if (t) {
+            A.row_exp[n] = (int8_t)(e + t);
+            atomicOr(A.fired, 1);
+            A.rowlist[atomicAdd(A.fired + 1, 1)] = (int32_t)n;
+        }
     } else if (i < A.N + A.K) {
         const int64_t k = i - A.N;
         const int32_t mx = A.col_max[k];
@@ -93,47 +98,65 @@ __global__ void reb_decide_kernel(RebArgs A) {
         }
         const int t = up - dn;
         A.ct[k] = (int8_t)t;
-        if (t) { A.col_exp[k] = (int8_t)(e + t); atomicOr(A.fired, 1); }
+        if (t) {
+            A.col_exp[k] = (int8_t)(e + t);
+            atomicOr(A.fired, 1);
+            A.collist[atomicAdd(A.fired + 2, 1)] = (int32_t)k;
+        }
     }
 }
 
+__device__ __forceinline__ void reb_shift_word(const RebArgs& A, int64_t n, int64_t k, int32_t sd, uint32_t NK) {
+    const int32_t net = (int32_t)A.rt[n] + (int32_t)A.ct[k];
+    if (net == 0) return;
+    int32_t* pw = A.packed + n * A.ldp + k;
+    const int32_t w = *pw;
+    const int32_t sf = w >> 16, ss = shl32(w, 16) >> 24, vs = shl32(w, 24) >> 24;
+    int32_t nsf, nss, nvs;
+    if (net < 0) {
+        const int l = -net;
+        nsf = shl32(sf, l); nss = shl32(ss, l); nvs = shl32(vs, l);
+    } else {
+        const int rsh = net;
+        const uint32_t off = (uint32_t)((A.row0 + n) * A.K + k);
+        const float two_pos = exp2i(rsh);
+        const int32_t q = sf >> rsh;
+        const float rem = (float)(sf - shl32(q, rsh));
+        const int32_t sfs = q + (__fmul_rn(tl_rand(sd, off), two_pos) < rem ? 1 : 0);
+        const int32_t qs = ss >> rsh;
+        const float rems = (float)(ss - shl32(qs, rsh));
+        const int32_t ssu = qs + (__fmul_rn(tl_rand(sd, off + NK), two_pos) < rems ? 1 : 0);
+        const int32_t sres = shl32(ss, 7 - rsh) - shl32(ssu, 7);
+        const int32_t qv = vs >> rsh;
+        const float remv = (float)(vs - shl32(qv, rsh));
+        const int32_t vu = qv + (__fmul_rn(tl_rand(sd, off + 2u * NK), two_pos) < remv ? 1 : 0);
+        const int32_t vres = shl32(vs, 7 - rsh) - shl32(vu, 7);
+        nsf = sfs + sres + vres; nss = ssu; nvs = vu;
+    }
+    *pw = repack(clampi(nsf, -32768, 32767), clampi(nss, -128, 127), clampi(nvs, -128, 127));
+}
+
+// Touches only words of a ticked row or a ticked column: first every column of
+// the ticked rows, then every other row of the ticked columns.
 __global__ void reb_shift_kernel(RebArgs A) {
-    const int32_t fired = *A.fired;
+    const int32_t fired = A.fired[0];
     if (A.fired_out && blockIdx.x == 0 && threadIdx.x == 0) *A.fired_out = fired;
     if (!fired) return;
     const int32_t sd = *A.seed;
     const uint32_t NK = (uint32_t)(A.N_total * A.K);
-    const int64_t total = A.N * A.K;
+    const int64_t nr = A.fired[1], nc = A.fired[2];
+    const int64_t rows_work = nr * A.K, total = rows_work + A.N * nc;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t n = i / A.K, k = i - n * A.K;
-        const int32_t net = (int32_t)A.rt[n] + (int32_t)A.ct[k];
-        if (net == 0) continue;
-        int32_t* pw = A.packed + n * A.ldp + k;
-        const int32_t w = *pw;
-        const int32_t sf = w >> 16, ss = shl32(w, 16) >> 24, vs = shl32(w, 24) >> 24;
-        int32_t nsf, nss, nvs;
-        if (net < 0) {
-            const int l = -net;
-            nsf = shl32(sf, l); nss = shl32(ss, l); nvs = shl32(vs, l);
+        if (i < rows_work) {
+            const int64_t n = A.rowlist[i / A.K];
+            reb_shift_word(A, n, i % A.K, sd, NK);
         } else {
-            const int rsh = net;
-            const uint32_t off = (uint32_t)((A.row0 + n) * A.K + k);
-            const float two_pos = exp2i(rsh);
-            const int32_t q = sf >> rsh;
-            const float rem = (float)(sf - shl32(q, rsh));
-            const int32_t sfs = q + (__fmul_rn(tl_rand(sd, off), two_pos) < rem ? 1 : 0);
-            const int32_t qs = ss >> rsh;
-            const float rems = (float)(ss - shl32(qs, rsh));
-            const int32_t ssu = qs + (__fmul_rn(tl_rand(sd, off + NK), two_pos) < rems ? 1 : 0);
-            const int32_t sres = shl32(ss, 7 - rsh) - shl32(ssu, 7);
-            const int32_t qv = vs >> rsh;
-            const float remv = (float)(vs - shl32(qv, rsh));
-            const int32_t vu = qv + (__fmul_rn(tl_rand(sd, off + 2u * NK), two_pos) < remv ? 1 : 0);
-            const int32_t vres = shl32(vs, 7 - rsh) - shl32(vu, 7);
-            nsf = sfs + sres + vres; nss = ssu; nvs = vu;
+            const int64_t j = i - rows_work;
+            const int64_t n = j / nc;
+            if (A.rt[n] != 0) continue;  // done in the row pass
+            reb_shift_word(A, n, A.collist[j % nc], sd, NK);
         }
-        *pw = repack(clampi(nsf, -32768, 32767), clampi(nss, -128, 127), clampi(nvs, -128, 127));
     }
 }
 
@@ -145,7 +168,8 @@ static size_t al256(size_t x) { return (x + 255) / 256 * 256; }
 
 extern "C" size_t concord_rebalance_workspace_bytes(int64_t N, int64_t K) {
     if (N <= 0 || K <= 0) return 0;
-    return 256 + al256((size_t)N) + al256((size_t)K) + al256((size_t)N * HB * 4) + al256((size_t)K * HB * 4);
+    return 256 + al256((size_t)N) + al256((size_t)K) + al256((size_t)N * HB * 4) + al256((size_t)K * HB * 4) +
+           al256((size_t)N * 4) + al256((size_t)K * 4);
 }
 
 extern "C" int concord_rebalance(int32_t* packed, int64_t ldp, int8_t* row_exp, int8_t* col_exp,
@@ -175,12 +199,14 @@ extern "C" int concord_rebalance(int32_t* packed, int64_t ldp, int8_t* row_exp, 
     A.ct = reinterpret_cast<int8_t*>(ws + 256 + al256((size_t)N));
     A.rhist = reinterpret_cast<int32_t*>(ws + 256 + al256((size_t)N) + al256((size_t)K));
     A.chist = reinterpret_cast<int32_t*>(ws + 256 + al256((size_t)N) + al256((size_t)K) + al256((size_t)N * HB * 4));
+    A.rowlist = reinterpret_cast<int32_t*>(reinterpret_cast<char*>(A.chist) + al256((size_t)K * HB * 4));
+    A.collist = reinterpret_cast<int32_t*>(reinterpret_cast<char*>(A.rowlist) + al256((size_t)N * 4));
     cudaStream_t s = as_stream(stream);
-    if (cudaMemsetAsync(A.fired, 0, sizeof(int32_t), s) != cudaSuccess) return check_launch("concord_rebalance");
+    if (cudaMemsetAsync(A.fired, 0, 3 * sizeof(int32_t), s) != cudaSuccess) return check_launch("concord_rebalance");
     int64_t blocks = (N * K + RB_THREADS - 1) / RB_THREADS;
     if (blocks > 148 * 32) blocks = 148 * 32;
     if (allow_tickdown) reb_hist_kernel<<<(unsigned)blocks, RB_THREADS, 0, s>>>(A);
     reb_decide_kernel<<<(unsigned)((N + K + RB_THREADS - 1) / RB_THREADS), RB_THREADS, 0, s>>>(A);
-    reb_shift_kernel<<<(unsigned)blocks, RB_THREADS, 0, s>>>(A);
+    reb_shift_kernel<<<148 * 4, RB_THREADS, 0, s>>>(A);
     return check_launch("concord_rebalance");
 }
