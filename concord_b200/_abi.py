@@ -125,6 +125,9 @@ _SIGS = [
     ("concord_vhat_workspace_bytes", ctypes.c_size_t, [_I64, _I64]),
     ("concord_vhat_update", ctypes.c_int,
      [_P, _I64, _I64, _I64, _P, _P, _P, _F, _F, _P, _P, _P, _P, ctypes.c_size_t, _P]),
+    ("concord_vhat_noalloc_max_scratch_bytes", ctypes.c_size_t, []),
+    ("concord_vhat_update_noalloc", ctypes.c_int,
+     [_P, _I64, _I64, _I64, _P, _P, _P, _F, _F, _P, _P, _P, _P]),
     ("concord_vhat_partial", ctypes.c_int,
      [_P, _I64, _I64, _I64, _P, _F, _F, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P]),
     ("concord_vhat_finish", ctypes.c_int, [_P, _P, _P, _P, _I64, _F, _F, _P]),

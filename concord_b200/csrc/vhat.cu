@@ -245,3 +245,71 @@ extern "C" int concord_vhat_finish(const float* col_sum, const float* vsum, floa
     vhat_finish_kernel<<<blocks, 256, 0, as_stream(stream)>>>(col_sum, vsum, v_col, sum_v_inv, K, beta2, one_minus_beta2);
     return check_launch("concord_vhat_finish");
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free form of concord_vhat_update.
+//
+// For callers that are not allowed to allocate device memory themselves: a
+// host framework that hands plugins a fixed device-memory budget and forbids
+// cudaMalloc after start-up, or a caller on a latency-critical path where the
+// implicit device synchronisation of cudaMalloc/cudaFree would stall other
+// streams.  The scratch lives in a file-scope device array that every GPU
+// loading this library holds until the process exits.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace concord {
+
+constexpr size_t VHAT_STATIC_SCRATCH_BYTES = 4u << 20;  // 4 MiB per device
+static __device__ __align__(256) unsigned char g_vhat_scratch[VHAT_STATIC_SCRATCH_BYTES];
+
+constexpr int MAX_DEVICES = 64;
+static void* g_vhat_scratch_ptr[MAX_DEVICES];  // device address of g_vhat_scratch, per device
+static std::mutex g_vhat_scratch_mu;
+
+// Once per device, with that device current: look up the array's device
+// address (the host-side name is only a stand-in) and clear it.
+static int vhat_scratch_for_current_device(void** out, cudaStream_t stream) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES)
+        return fail(CONCORD_ENODEVICE, "concord_vhat_update_noalloc: no usable current CUDA device");
+    std::lock_guard<std::mutex> lock(g_vhat_scratch_mu);
+    if (!g_vhat_scratch_ptr[dev]) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_vhat_scratch);
+        if (e != cudaSuccess || !p)
+            return fail(CONCORD_ELAUNCH, std::string("concord_vhat_update_noalloc: cudaGetSymbolAddress failed: ") +
+                                             cudaGetErrorString(e));
+        e = cudaMemsetAsync(p, 0, VHAT_STATIC_SCRATCH_BYTES, stream);
+        if (e != cudaSuccess)
+            return fail(CONCORD_ELAUNCH, std::string("concord_vhat_update_noalloc: clearing scratch failed: ") +
+                                             cudaGetErrorString(e));
+        g_vhat_scratch_ptr[dev] = p;
+    }
+    *out = g_vhat_scratch_ptr[dev];
+    return CONCORD_OK;
+}
+
+}  // namespace concord
+
+extern "C" size_t concord_vhat_noalloc_max_scratch_bytes(void) { return concord::VHAT_STATIC_SCRATCH_BYTES; }
+
+extern "C" int concord_vhat_update_noalloc(const uint16_t* grad, int64_t ldg, int64_t N, int64_t K,
+                                           float* v_row, float* v_col, float* sum_v_inv, float beta2,
+                                           float one_minus_beta2, int32_t* row_max, int32_t* col_max,
+                                           int32_t* salt, void* stream) {
+    if (!grad || !v_row || !v_col || !sum_v_inv)
+        return fail(CONCORD_EINVAL, "concord_vhat_update_noalloc: null pointer");
+    if (N <= 0 || K <= 0 || ldg < K) return fail(CONCORD_ESHAPE, "concord_vhat_update_noalloc: bad shape/stride");
+    const size_t need = concord_vhat_workspace_bytes(N, K);
+    if (need > concord::VHAT_STATIC_SCRATCH_BYTES)
+        return fail(CONCORD_ETOOBIG, "concord_vhat_update_noalloc: N x K needs " + std::to_string(need) +
+                                         " bytes of scratch, above the fixed 4 MiB per device; use "
+                                         "concord_vhat_update with a caller-provided workspace");
+    void* ws = nullptr;
+    int rc = concord::vhat_scratch_for_current_device(&ws, as_stream(stream));
+    if (rc != CONCORD_OK) return rc;
+    return vhat_launch(grad, ldg, N, K, v_row, v_col, sum_v_inv, beta2, one_minus_beta2, row_max, col_max, salt,
+                       nullptr, nullptr, ws, concord::VHAT_STATIC_SCRATCH_BYTES, stream,
+                       "concord_vhat_update_noalloc");
+}

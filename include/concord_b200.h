@@ -129,6 +129,29 @@ int concord_vhat_update(const uint16_t* grad, int64_t ldg, int64_t N, int64_t K,
                         void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * concord_vhat_update without a caller-provided workspace.  No counterpart in
+ * the reference.  For callers that may not allocate device memory (a host
+ * framework that owns all device memory behind a fixed budget, or a
+ * latency-critical caller that cannot afford cudaMalloc's implicit device
+ * synchronisation): the scratch is a fixed 4 MiB array inside this library
+ * (concord_vhat_noalloc_max_scratch_bytes()), held by every GPU that loads
+ * the library until the process exits.  Sizes whose
+ * concord_vhat_workspace_bytes(N, K) exceed it are rejected with
+ * CONCORD_ETOOBIG.  The first call on a device, with that device current,
+ * looks up the array's device address and clears it on `stream`; make that
+ * first call before any stream capture.  All calls on a device share the one
+ * array: calls that may overlap on the GPU (different streams without
+ * ordering) race and must be serialised by the caller.  Nothing else differs
+ * from concord_vhat_update: same results, bit for bit.
+ */
+size_t concord_vhat_noalloc_max_scratch_bytes(void);
+int concord_vhat_update_noalloc(const uint16_t* grad, int64_t ldg, int64_t N, int64_t K,
+                                float* v_row, float* v_col, float* sum_v_inv,
+                                float beta2, float one_minus_beta2,
+                                int32_t* row_max, int32_t* col_max, int32_t* salt,
+                                void* stream);
+
+/*
  * Row-sharded form of concord_vhat_update for data-parallel training
  * (the reference has no multi-GPU code; this splits its v-hat update,
  * packed_b.py:1288-1303, at the one point that needs all rows).  On this
