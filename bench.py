@@ -106,7 +106,8 @@ def setup_layer(n_rows, k_cols, device, seed=0):
 
 
 def make_grads(n_rows, k_cols, device, count=2, seed=1):
-    """dW = dY^T X (bf16) for `count` synthetic batches; also times the GEMMs."""
+    """dW = dY^T X (bf16) for `count` synthetic batches; also times the layer's
+    GEMMs (this package's tcgen05 kernels, and cuBLAS through torch beside them)."""
     from concord_b200 import gemm
     g = torch.Generator(device=device).manual_seed(seed)
     grads, gemm_ms = [], {}
@@ -117,7 +118,9 @@ def make_grads(n_rows, k_cols, device, count=2, seed=1):
         if i == 0:
             W = torch.randn(n_rows, k_cols, device=device, dtype=torch.bfloat16) * 0.02
             for name, fn in (("fwd", lambda: gemm.forward(X, W)), ("dx", lambda: gemm.grad_input(dY, W)),
-                             ("dw", lambda: gemm.grad_weight(dY, X))):
+                             ("dw", lambda: gemm.grad_weight(dY, X)),
+                             ("cublas_fwd", lambda: X @ W.T), ("cublas_dx", lambda: dY @ W),
+                             ("cublas_dw", lambda: dY.T @ X)):
                 for _ in range(3):
                     fn()
                 s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -331,7 +334,7 @@ def main():
                      "kernel_ms": r["step_kernel_ms"]},
         "vhat_ms": r["vhat_ms"],
         "gemm": {k: {"ms": v, "tflops": flops / (v * 1e-3) / 1e12} for k, v in r["gemm_ms"].items()},
-        "gemm_impl": "cuBLAS via torch (library)",
+        "gemm_impl": "fwd/dx/dw: concord tcgen05 kernels (CUTLASS sm100 templates); cublas_*: torch",
         "clocks": r["clocks"],
         "gpu_launches": args.steps * 4,
         "gpu_launches_note": "per step: vhat 1 + step 1 + rebalance decide 1 + shift 1 (+1 memset node)",

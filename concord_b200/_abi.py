@@ -143,6 +143,10 @@ _SIGS = [
     ("concord_quantize", ctypes.c_int,
      [_P, _I64, _P, _I64, _P, _P, _I64, _I64, _I32, _I32, _I32, _I32, _P]),
     ("concord_coherence", ctypes.c_int, [_P, _I64, _I64, _I64, _F, _P, _P]),
+    ("concord_gemm_workspace_bytes", ctypes.c_size_t, [_I64, _I64, _I64]),
+    ("concord_gemm_fwd", ctypes.c_int, [_P, _P, _P, _I64, _I64, _I64, _P, ctypes.c_size_t, _P]),
+    ("concord_gemm_dx", ctypes.c_int, [_P, _P, _P, _I64, _I64, _I64, _P, ctypes.c_size_t, _P]),
+    ("concord_gemm_dw", ctypes.c_int, [_P, _P, _P, _I64, _I64, _I64, _P, ctypes.c_size_t, _P]),
 ]
 
 EXPORTED = [s[0] for s in _SIGS]

@@ -24,6 +24,29 @@ NVFLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-fmad=false", "-Xcompiler",
                   "-Xcompiler", "-ffp-contract=off", "--expt-relaxed-constexpr"]
 
 
+def _cutlass_root():
+    """CUTLASS/CuTe headers (a vendored header tree shipped inside flashinfer)."""
+    env = os.environ.get("CUTLASS_DIR")
+    if env:
+        return env
+    import importlib.util
+    spec = importlib.util.find_spec("flashinfer")
+    if spec is None or not spec.submodule_search_locations:
+        raise RuntimeError("CUTLASS headers not found: set CUTLASS_DIR")
+    return os.path.join(list(spec.submodule_search_locations)[0], "data", "cutlass")
+
+
+def _flags_for(cu):
+    if os.path.basename(cu) == "gemm.cu":
+        root = _cutlass_root()
+        # tensor-core GEMMs: contraction order is the hardware's; no -fmad=false needed
+        return ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
+                       "-I" + os.path.join(root, "include"),
+                       "-I" + os.path.join(root, "tools", "util", "include"),
+                       "-DNDEBUG", "-Xcompiler", "-Wno-psabi", "-diag-suppress", "20012"]
+    return NVFLAGS
+
+
 def _newer(target, deps):
     if not os.path.exists(target):
         return True
@@ -42,7 +65,7 @@ def build(verbose=False, force=False):
         obj = os.path.join(objdir, os.path.basename(cu) + ".o")
         objs.append(obj)
         if force or _newer(obj, [cu] + headers):
-            cmd = [NVCC] + NVFLAGS + ["-c", cu, "-o", obj]
+            cmd = [NVCC] + _flags_for(cu) + ["-c", cu, "-o", obj]
             if verbose:
                 print(" ".join(cmd), flush=True)
             subprocess.check_call(cmd)

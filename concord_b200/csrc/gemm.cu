@@ -1,0 +1,136 @@
+// gemm.cu — the layer's dense GEMMs on B200 tensor cores (tcgen05 / TMEM / TMA).
+//
+// Replaces the cuBLAS calls of the reference layer (concord/packed_b.py:1219
+// forward F.linear, 1263 dX = dY W, 1273 dW = dY^T X):
+//   fwd: Y[M,N]  = X[M,K]  * W[N,K]^T       (A row-major,    B K-major)
+//   dX : DX[M,K] = DY[M,N] * W[N,K]         (A row-major,    B N-major)
+//   dW : DW[N,K] = DY[M,N]^T * X[M,K]       (A column-major, B row-major)
+// bf16 operands, fp32 accumulation in tensor memory, bf16 result rounded to
+// nearest even — the reference's numerics (its dW is rounded to bf16 before
+// the optimizer reads it, packed_b.py:1274-1277).
+//
+// Each GEMM is a CUTLASS 4 sm100 warp-specialised kernel instantiated here:
+// TMA producer warp -> shared-memory ring -> one thread issuing
+// tcgen05.mma (cta_group::1, 128x256x64 tiles) into TMEM -> epilogue warps
+// reading TMEM with tcgen05.ld and storing through TMA.  Cluster shape 1x1x1:
+// no TMA multicast is used anywhere (the same kernels run in multi-GPU jobs).
+#include <cuda_runtime.h>
+
+#include "cute/tensor.hpp"
+#include "cutlass/cutlass.h"
+#include "cutlass/epilogue/collective/collective_builder.hpp"
+#include "cutlass/gemm/collective/collective_builder.hpp"
+#include "cutlass/gemm/device/gemm_universal_adapter.h"
+#include "cutlass/gemm/kernel/gemm_universal.hpp"
+#include "cutlass/util/packed_stride.hpp"
+
+#include "../../include/concord_b200.h"
+
+namespace concord {
+int fail(int code, const std::string& msg);
+}
+
+namespace {
+
+using namespace cute;
+
+using BF16 = cutlass::bfloat16_t;
+using Acc = float;
+using TileMNK = Shape<_128, _256, _64>;
+using Cluster = Shape<_1, _1, _1>;
+
+using LayoutC = cutlass::layout::RowMajor;
+constexpr int kAlign = 8;  // 16 bytes of bf16
+
+using Epi = typename cutlass::epilogue::collective::CollectiveBuilder<
+    cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, TileMNK, Cluster,
+    cutlass::epilogue::collective::EpilogueTileAuto, Acc, Acc, BF16, LayoutC, kAlign, BF16, LayoutC, kAlign,
+    cutlass::epilogue::TmaWarpSpecialized1Sm>::CollectiveOp;
+constexpr int kEpiSmem = static_cast<int>(sizeof(typename Epi::SharedStorage));
+
+#define CONCORD_DEFINE_GEMM(NAME, LA, LB)                                                                    \
+    using NAME##Main = typename cutlass::gemm::collective::CollectiveBuilder<                               \
+        cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, BF16, LA, kAlign, BF16, LB, kAlign, Acc,    \
+        TileMNK, Cluster, cutlass::gemm::collective::StageCountAutoCarveout<kEpiSmem>,                      \
+        cutlass::gemm::KernelTmaWarpSpecialized1SmSm100>::CollectiveOp;                                    \
+    using NAME##Kernel = cutlass::gemm::kernel::GemmUniversal<Shape<int, int, int, int>, NAME##Main, Epi, void>; \
+    using NAME = cutlass::gemm::device::GemmUniversalAdapter<NAME##Kernel>;
+
+CONCORD_DEFINE_GEMM(GemmFwd, cutlass::layout::RowMajor, cutlass::layout::ColumnMajor)
+CONCORD_DEFINE_GEMM(GemmDx, cutlass::layout::RowMajor, cutlass::layout::RowMajor)
+CONCORD_DEFINE_GEMM(GemmDw, cutlass::layout::ColumnMajor, cutlass::layout::RowMajor)
+
+// D[m,n] = sum_k A[m,k] B[k,n]; strides from the problem's layouts.
+template <class Gemm>
+int run_gemm(const void* A, const void* B, void* D, int M, int N, int K, void* workspace, size_t ws_bytes,
+             cudaStream_t stream, bool query_only, size_t* ws_needed, const char* name) {
+    using StrideA = typename Gemm::GemmKernel::StrideA;
+    using StrideB = typename Gemm::GemmKernel::StrideB;
+    using StrideC = typename Gemm::GemmKernel::StrideC;
+    using StrideD = typename Gemm::GemmKernel::StrideD;
+    StrideA sa = cutlass::make_cute_packed_stride(StrideA{}, cute::make_shape(M, K, 1));
+    StrideB sb = cutlass::make_cute_packed_stride(StrideB{}, cute::make_shape(N, K, 1));
+    StrideC sc = cutlass::make_cute_packed_stride(StrideC{}, cute::make_shape(M, N, 1));
+    StrideD sd = cutlass::make_cute_packed_stride(StrideD{}, cute::make_shape(M, N, 1));
+    typename Gemm::Arguments args{
+        cutlass::gemm::GemmUniversalMode::kGemm,
+        {M, N, K, 1},
+        {reinterpret_cast<const BF16*>(A), sa, reinterpret_cast<const BF16*>(B), sb},
+        {{1.0f, 0.0f}, reinterpret_cast<const BF16*>(D), sc, reinterpret_cast<BF16*>(D), sd}};
+    Gemm gemm;
+    if (query_only) {
+        *ws_needed = Gemm::get_workspace_size(args);
+        return CONCORD_OK;
+    }
+    if (gemm.can_implement(args) != cutlass::Status::kSuccess)
+        return concord::fail(CONCORD_ESHAPE, std::string(name) + ": shape/alignment not supported "
+                                             "(every extent must be a multiple of 8)");
+    if (Gemm::get_workspace_size(args) > ws_bytes)
+        return concord::fail(CONCORD_EWORKSPACE, std::string(name) + ": workspace too small");
+    if (gemm.initialize(args, workspace, stream) != cutlass::Status::kSuccess)
+        return concord::fail(CONCORD_ELAUNCH, std::string(name) + ": initialize failed");
+    if (gemm.run(stream) != cutlass::Status::kSuccess)
+        return concord::fail(CONCORD_ELAUNCH, std::string(name) + ": launch failed");
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return concord::fail(CONCORD_ELAUNCH, std::string(name) + ": " + cudaGetErrorString(e));
+    return CONCORD_OK;
+}
+
+bool bad(const void* p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) % 16) != 0; }
+
+}  // namespace
+
+// Y[M,N] = X[M,K] W[N,K]^T
+extern "C" int concord_gemm_fwd(const uint16_t* x, const uint16_t* w, uint16_t* y, int64_t M, int64_t N, int64_t K,
+                                void* workspace, size_t workspace_bytes, void* stream) {
+    if (bad(x) || bad(w) || bad(y)) return concord::fail(CONCORD_EALIGN, "concord_gemm_fwd: null or unaligned pointer");
+    if (M <= 0 || N <= 0 || K <= 0) return concord::fail(CONCORD_ESHAPE, "concord_gemm_fwd: bad shape");
+    return run_gemm<GemmFwd>(x, w, y, (int)M, (int)N, (int)K, workspace, workspace_bytes,
+                             reinterpret_cast<cudaStream_t>(stream), false, nullptr, "concord_gemm_fwd");
+}
+
+// DX[M,K] = DY[M,N] W[N,K]   (GEMM m=M, n=K, k=N)
+extern "C" int concord_gemm_dx(const uint16_t* dy, const uint16_t* w, uint16_t* dx, int64_t M, int64_t N, int64_t K,
+                               void* workspace, size_t workspace_bytes, void* stream) {
+    if (bad(dy) || bad(w) || bad(dx)) return concord::fail(CONCORD_EALIGN, "concord_gemm_dx: null or unaligned pointer");
+    if (M <= 0 || N <= 0 || K <= 0) return concord::fail(CONCORD_ESHAPE, "concord_gemm_dx: bad shape");
+    return run_gemm<GemmDx>(dy, w, dx, (int)M, (int)K, (int)N, workspace, workspace_bytes,
+                            reinterpret_cast<cudaStream_t>(stream), false, nullptr, "concord_gemm_dx");
+}
+
+// DW[N,K] = DY[M,N]^T X[M,K]   (GEMM m=N, n=K, k=M)
+extern "C" int concord_gemm_dw(const uint16_t* dy, const uint16_t* x, uint16_t* dw, int64_t M, int64_t N, int64_t K,
+                               void* workspace, size_t workspace_bytes, void* stream) {
+    if (bad(dy) || bad(x) || bad(dw)) return concord::fail(CONCORD_EALIGN, "concord_gemm_dw: null or unaligned pointer");
+    if (M <= 0 || N <= 0 || K <= 0) return concord::fail(CONCORD_ESHAPE, "concord_gemm_dw: bad shape");
+    return run_gemm<GemmDw>(dy, x, dw, (int)N, (int)K, (int)M, workspace, workspace_bytes,
+                            reinterpret_cast<cudaStream_t>(stream), false, nullptr, "concord_gemm_dw");
+}
+
+extern "C" size_t concord_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+    size_t a = 0, b = 0, c = 0;
+    run_gemm<GemmFwd>(nullptr, nullptr, nullptr, (int)M, (int)N, (int)K, nullptr, 0, nullptr, true, &a, "");
+    run_gemm<GemmDx>(nullptr, nullptr, nullptr, (int)M, (int)K, (int)N, nullptr, 0, nullptr, true, &b, "");
+    run_gemm<GemmDw>(nullptr, nullptr, nullptr, (int)N, (int)K, (int)M, nullptr, 0, nullptr, true, &c, "");
+    return std::max(a, std::max(b, c));
+}

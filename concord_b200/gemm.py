@@ -1,22 +1,86 @@
 """Dense GEMMs around the packed step: forward Y = X W^T, dX = dY W, dW = dY^T X.
 
-These are plain bf16 library GEMMs (cuBLAS via torch) with fp32
-accumulation, as in the reference (packed_b.py:1219, 1263, 1273).
+bf16 operands, fp32 accumulation, bf16 results (the reference's numerics,
+packed_b.py:1219, 1263, 1271-1277).  Shapes whose extents are multiples of 8
+run this package's tcgen05/TMEM kernels (`concord_gemm_*` in the C ABI);
+other shapes (tiny or odd layers) use torch's cuBLAS matmul, as the
+reference does for every shape.
 """
+import ctypes
+
 import torch
 import torch.nn.functional as F
 
+from . import _abi
+
+_WS = {}
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _ok(*dims):
+    return all(int(d) % 8 == 0 for d in dims)
+
+
+def _workspace(M, N, K, device):
+    lib = _abi.load()
+    need = lib.concord_gemm_workspace_bytes(M, N, K)
+    key = str(device)
+    buf = _WS.get(key)
+    if buf is None or buf.numel() < max(need, 1):
+        buf = torch.empty(max(need, 256), dtype=torch.uint8, device=device)
+        _WS[key] = buf
+    return buf
+
+
+def _run(fn, a, b, out, M, N, K):
+    lib = _abi.load()
+    ws = _workspace(M, N, K, out.device)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(out.device).cuda_stream)
+    _abi.check(getattr(lib, fn)(_ptr(a), _ptr(b), _ptr(out), M, N, K, _ptr(ws), ws.numel(), stream), fn)
+    return out
+
+
+def _usable(*ts):
+    return all(t.is_cuda and t.dtype == torch.bfloat16 for t in ts)
+
 
 def forward(x, weight_bf16, bias=None):
+    """y = x W^T (+ bias) over the last dim of x."""
+    N, K = weight_bf16.shape
+    x2 = x.reshape(-1, K)
+    M = x2.shape[0]
+    if _usable(x2, weight_bf16) and _ok(M, N, K) and M > 0:
+        x2 = x2.contiguous()
+        y = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
+        _run("concord_gemm_fwd", x2, weight_bf16.contiguous(), y, M, N, K)
+        if bias is not None:
+            y.add_(bias)
+        return y.reshape(*x.shape[:-1], N)
     return F.linear(x, weight_bf16, bias)
 
 
 def grad_input(grad_y, weight_bf16):
+    """dX = dY W over the last dim of dY."""
+    N, K = weight_bf16.shape
+    g2 = grad_y.reshape(-1, N)
+    M = g2.shape[0]
+    if _usable(g2, weight_bf16) and _ok(M, N, K) and M > 0:
+        dx = torch.empty(M, K, dtype=torch.bfloat16, device=grad_y.device)
+        _run("concord_gemm_dx", g2.contiguous(), weight_bf16.contiguous(), dx, M, N, K)
+        return dx.reshape(*grad_y.shape[:-1], K)
     return grad_y @ weight_bf16
 
 
 def grad_weight(grad_y_flat, x_flat):
     """dW = dY^T X rounded to bf16, contiguous [N, K]."""
+    M, N = grad_y_flat.shape
+    K = x_flat.shape[1]
+    if _usable(grad_y_flat, x_flat) and _ok(M, N, K) and M > 0:
+        dw = torch.empty(N, K, dtype=torch.bfloat16, device=x_flat.device)
+        return _run("concord_gemm_dw", grad_y_flat.contiguous(), x_flat.contiguous(), dw, M, N, K)
     g = grad_y_flat.transpose(0, 1) @ x_flat
     if g.dtype != torch.bfloat16:
         g = g.to(torch.bfloat16)

@@ -37,6 +37,8 @@
  *                            load_weights_finetune (1816-1856)
  *   concord_coherence     <- measure_coherence / gate_coherence_from_fields
  *                            (packed_b.py:2081-2106)
+ *   concord_gemm_fwd/dx/dw <- F.linear / grad_y @ W / grad_y^T @ x
+ *                            (packed_b.py:1219, 1263, 1271-1277)
  */
 #ifndef CONCORD_B200_H
 #define CONCORD_B200_H
@@ -236,6 +238,24 @@ int concord_quantize(const float* W, int64_t ldw, int32_t* packed, int64_t ldp,
  */
 int concord_coherence(const int32_t* packed, int64_t ldp, int64_t N, int64_t K,
                       float drift_cancel_C, double* out, void* stream);
+
+/*
+ * The layer's dense GEMMs on the tensor cores (tcgen05/TMEM, TMA-fed), bf16
+ * in, fp32 accumulate, bf16 out (round to nearest even).  Row-major,
+ * contiguous operands; every extent a multiple of 8 and 16-byte aligned
+ * pointers (else CONCORD_ESHAPE / CONCORD_EALIGN).
+ *   concord_gemm_fwd: y[M,N]  = x[M,K] * w[N,K]^T        (F.linear without bias)
+ *   concord_gemm_dx:  dx[M,K] = dy[M,N] * w[N,K]
+ *   concord_gemm_dw:  dw[N,K] = dy[M,N]^T * x[M,K]
+ * Workspace: concord_gemm_workspace_bytes(M, N, K) (may be 0).
+ */
+size_t concord_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K);
+int concord_gemm_fwd(const uint16_t* x, const uint16_t* w, uint16_t* y, int64_t M, int64_t N, int64_t K,
+                     void* workspace, size_t workspace_bytes, void* stream);
+int concord_gemm_dx(const uint16_t* dy, const uint16_t* w, uint16_t* dx, int64_t M, int64_t N, int64_t K,
+                    void* workspace, size_t workspace_bytes, void* stream);
+int concord_gemm_dw(const uint16_t* dy, const uint16_t* x, uint16_t* dw, int64_t M, int64_t N, int64_t K,
+                    void* workspace, size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }
