@@ -39,7 +39,10 @@ def test_gemm_batched_input_and_bias():
     b = torch.randn(512, generator=g, device=DEV).to(torch.bfloat16)
     y = gemm.forward(x, w, b)
     assert y.shape == (4, 64, 512)
-    _close(y, (x.float() @ w.float().T + b.float()))
+    xw = x.float() @ w.float().T
+    # two bf16 roundings (product, then + bias): bound by the operands' size
+    err = (y.float() - (xw + b.float())).abs()
+    assert bool((err <= (xw.abs() + b.float().abs()) * 2.0 ** -7 + 1e-6).all())
 
 
 def test_gemm_native_kernel_is_used():
