@@ -240,3 +240,33 @@ def test_coherence_meter(pb, oracle_mod):
     s = coherence_sum(lay.packed_w, float(z["coh_C"])).cpu().numpy()
     ref = oracle_mod.coherence(z["coh_packed"], float(z["coh_C"]))
     assert s[1] == ref[1] and abs(s[0] - ref[0]) < 1e-9 * ref[1]
+
+
+@pytest.mark.parametrize("lr", [5e-5, 0.05, 2.0])
+def test_step_fast_tick_deferral_paths(pb, oracle_mod, lr):
+    """The step kernel decides most first ticks from a bounded fast denominator
+    and recomputes the undecided elements exactly; a large lr makes |delta_t|
+    large, so many (or, at lr=2, most) elements take the deferred or the
+    list-overflow path.  Words must stay bit-exact whatever the split."""
+    rng = np.random.default_rng(int(lr * 1e5) + 7)
+    N, K = 300, 512
+    z = load("step_bare")
+    P = params_of(z)
+    packed = random_state(rng, N, K)
+    grad = oracle_mod.f32_to_bf16(rng.normal(0, 1e-2, (N, K)).astype(np.float32))
+    rexp = rng.integers(-6, 3, N).astype(np.int8)
+    cexp = rng.integers(-2, 3, K).astype(np.int8)
+    v_row = (rng.random(N) * 1e-4 + 1e-7).astype(np.float32)
+    v_col = (rng.random(K) * 1e-4 + 1e-7).astype(np.float32)
+    svi = np.array([1.0 / v_row.sum()], np.float32)
+    coh_pre = rng.random((N, K)).astype(np.float32)
+    got = run_cuda_step(pb, P, packed, grad, rexp, cexp, v_row, v_col, svi, coh_pre, lr, 1e-10, 99)
+    ref_p, ref_w = packed.copy(), np.zeros((N, K), np.uint16)
+    ref_rm, ref_cm, ref_cp = np.zeros(N, np.int32), np.zeros(K, np.int32), coh_pre.copy()
+    oracle_mod.step(P, ref_p, grad, ref_w, rexp, cexp, ref_rm, ref_cm, v_row, v_col, svi, ref_cp,
+                    lr, 1e-10, 99)
+    np.testing.assert_array_equal(got[0], ref_p)
+    np.testing.assert_array_equal(got[1], ref_w)
+    np.testing.assert_array_equal(got[2], ref_rm)
+    np.testing.assert_array_equal(got[3], ref_cm)
+    np.testing.assert_array_equal(got[4], ref_cp)
