@@ -110,36 +110,28 @@ __device__ __forceinline__ void fixed_coh_divide(const concord_step_params& P, A
 }
 
 // Second half (packed_b.py:558-703), given denom_p = exp2(p*log2(x)).
-// delta_t of the first SR tick from step_div = g / denom_p (packed_b.py:558-591):
-// a monotone chain of single-rounded fp32 ops in step_div
 template <uint32_t FL, bool SAFE = false>
-__device__ __forceinline__ float adamw_delta(const concord_step_params& P, const AdamwPre& e, float step_div,
-                                             const StepScalars& S) {
+__device__ __forceinline__ ElemOut adamw_post(const concord_step_params& P, const AdamwPre& e,
+                                              float step_div, const StepScalars& S, int32_t pos) {
     const uint32_t F = flags_of<FL>(P);
+    const float scale_fwd = pow2_exp<SAFE>(e.te);
     const float scale_inv = pow2_exp<SAFE>(-e.te);
-    const float d_fs = e.d_fs;
-    float step_live = clamp_np(step_div, P.step_cap);
+    const float coh = e.coh, d_fs = e.d_fs;
+    int32_t s_fast = e.s_fast, s_slow = e.s_slow;
+    const int32_t v_slow = e.v_slow;
+    float step_live = clamp_np(step_div, P.step_cap);  // step_div = g / denom_p
     const bool consol = (F & CONCORD_F_GF_CONSOL) != 0;
     float evap = 0.0f;
     if (consol) {
-        evap = S.lr * P.gf_consol * (1.0f - e.coh) * d_fs;
+        evap = S.lr * P.gf_consol * (1.0f - coh) * d_fs;
     } else {
-        step_live = step_live + P.weight_decay * (d_fs * pow2_exp<SAFE>(e.te));
+        step_live = step_live + P.weight_decay * (d_fs * scale_fwd);
     }
     float delta_t = -S.lr * step_live * scale_inv - P.beta1 * d_fs;
     if (consol) delta_t = delta_t - evap;
-    return delta_t;
-}
 
-// Everything after the first SR tick (packed_b.py:601-703), given s_fast after it.
-template <uint32_t FL, bool SAFE = false>
-__device__ __forceinline__ ElemOut adamw_rest(const concord_step_params& P, const AdamwPre& e,
-                                              int32_t s_fast, const StepScalars& S, int32_t pos) {
-    const uint32_t F = flags_of<FL>(P);
-    const float scale_fwd = pow2_exp<SAFE>(e.te);
-    const float coh = e.coh;
-    int32_t s_slow = e.s_slow;
-    const int32_t v_slow = e.v_slow;
+    s_fast = s_fast + sr_tick(delta_t, hash_uniform(s_fast, pos, S.salt));
+
     int32_t new_v = v_slow;
     float cp_new = e.cp;
     if (F & CONCORD_F_APPLY_CHASE) {
@@ -187,70 +179,6 @@ __device__ __forceinline__ ElemOut adamw_rest(const concord_step_params& P, cons
     o.coh = coh;
     o.coh_pre = cp_new;
     return o;
-}
-
-template <uint32_t FL, bool SAFE = false>
-__device__ __forceinline__ ElemOut adamw_post(const concord_step_params& P, const AdamwPre& e,
-                                              float step_div, const StepScalars& S, int32_t pos) {
-    const float delta_t = adamw_delta<FL, SAFE>(P, e, step_div, S);
-    const int32_t s_fast = e.s_fast + sr_tick(delta_t, hash_uniform(e.s_fast, pos, S.salt));
-    return adamw_rest<FL, SAFE>(P, e, s_fast, S, pos);
-}
-
-// ---- fast first tick ------------------------------------------------------
-// The denominator exp2(p*log2(x)) feeds only the first SR tick.  Instead of
-// the correctly rounded evaluation, the hot path takes the hardware
-// approximations lg2.approx / ex2.approx, bounds how far the reference's
-// CR(2^(RN(p*CR(log2 x)))) can be from that estimate, pushes the whole
-// interval of possible step values through the (monotone, single-rounded)
-// fp32 chain to delta_t, and keeps the tick only when floor(delta_t) and the
-// SR comparison are the same over the whole interval.  Otherwise (about one
-// element in 10^3 at lr 5e-4) the element is recomputed exactly later.
-// Error bounds used (checked exhaustively on B200 over every fp32 input):
-//   |lg2.approx(m) - log2(m)| < 2^-21 for m in [1, 2);
-//   |ex2.approx(y) / 2^y - 1|  < 2^-22.7 for y in [-125, 127).
-__device__ __forceinline__ float lg2_approx(float x) {
-    float r;
-    asm("lg2.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
-    return r;
-}
-__device__ __forceinline__ float ex2_approx(float x) {
-    float r;
-    asm("ex2.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
-    return r;
-}
-
-// Returns true (and the tick) when the first SR tick is decided.
-template <uint32_t FL>
-__device__ __forceinline__ bool fast_first_tick(const concord_step_params& P, const AdamwPre& e,
-                                                const StepScalars& S, int32_t pos, int32_t* tick) {
-    const uint32_t ix = __float_as_uint(e.x);
-    if (ix - 0x00800000u >= 0x7F000000u) return false;     // x not a positive normal
-    const int k = (int)(ix >> 23) - 127;
-    const float m = __uint_as_float((ix & 0x007fffffu) | 0x3f800000u);
-    const float p = P.precond_p;
-    const float yf = fmaf(p, lg2_approx(m), p * (float)k);
-    if (!(yf >= -125.0f && yf < 127.0f)) return false;
-    const float Df = ex2_approx(yf);
-    // |y_ref - yf| <= |p| 2^-21 (lg2) + |p| (|k|+1) 2^-22 (four roundings of y and L)
-    const float ap = fabsf(p);
-    const float dy = ap * 4.8e-7f + ap * (float)(abs(k) + 1) * 2.4e-7f;
-    // relative distance of D_ref from Df, then of RN(g/D_ref) from RN(g/Df), with margin
-    const float eps = dy * 0.6932f + 2.2e-7f;
-    const float e2 = eps * 1.01f + 4.0e-7f;
-    const float sm = e.g / Df;
-    const float a = sm * (1.0f - e2), b = sm * (1.0f + e2);
-    const float d1 = adamw_delta<FL, true>(P, e, a, S);
-    const float d2 = adamw_delta<FL, true>(P, e, b, S);
-    const float dlo = fminf(d1, d2), dhi = fmaxf(d1, d2);
-    if (!(fabsf(dlo) < 1.0e30f && fabsf(dhi) < 1.0e30f)) return false;   // NaN / huge
-    const float fl = floorf(dlo);
-    if (floorf(dhi) != fl) return false;
-    const float r = hash_uniform(e.s_fast, pos, S.salt);
-    const bool up = r < __fsub_rn(dlo, fl);
-    if (up != (r < __fsub_rn(dhi, fl))) return false;
-    *tick = __float2int_rz(__fadd_rn(fl, up ? 1.0f : 0.0f));
-    return true;
 }
 
 // One element of the AdamW-path step (packed_b.py:476-703).
@@ -369,16 +297,8 @@ __device__ __forceinline__ ElemOut step_elem(const concord_step_params& P, int32
 
 // Vector path: K % 4 == 0, row strides % 4 == 0, 16-byte aligned bases.
 // Block = 8 warps; each warp covers 128 columns (4 per lane) of 8 rows.
-constexpr int DEF_CAP = 1024;  // deferred elements per block (shared-memory list)
-
-template <int KIND, uint32_t FL, int MINB, bool FAST>
+template <int KIND, uint32_t FL, int MINB>
 __global__ void __launch_bounds__(STEP_THREADS, MINB) step_vec_kernel(StepArgs A) {
-    __shared__ int4 s_def[FAST ? DEF_CAP : 1];
-    __shared__ int s_ndef;
-    if (FAST) {
-        if (threadIdx.x == 0) s_ndef = 0;
-        __syncthreads();
-    }
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int64_t k0 = (int64_t)blockIdx.x * STEP_COLS + lane * VEC;
     const bool active = k0 < A.K;
@@ -468,42 +388,12 @@ __global__ void __launch_bounds__(STEP_THREADS, MINB) step_vec_kernel(StepArgs A
                 }
 #pragma unroll
                 for (int j = 0; j < VEC; ++j) fixed_coh_divide<FL>(A.P, pre[j]);
-                if (FAST) {
-                    // first tick from the bounded fast denominator; undecided
-                    // elements are recomputed exactly after the row loop
-                    int32_t t1[VEC];
-                    bool ok[VEC];
+                crmath::cr_pow2log2<VEC>(xs, A.P.precond_p, den);
 #pragma unroll
-                    for (int j = 0; j < VEC; ++j)
-                        ok[j] = fast_first_tick<FL>(A.P, pre[j], S, posn ^ (int32_t)(k0 + j), &t1[j]);
+                for (int j = 0; j < VEC; ++j) den[j] = pre[j].g / den[j];
 #pragma unroll
-                    for (int j = 0; j < VEC; ++j) {
-                        const int32_t pos = posn ^ (int32_t)(k0 + j);
-                        if (ok[j]) {
-                            outs[j] = adamw_rest<FL, true>(A.P, pre[j], pre[j].s_fast + t1[j], S, pos);
-                        } else {
-                            const int slot = atomicAdd(&s_ndef, 1);
-                            if (slot < DEF_CAP) {
-                                s_def[slot] = make_int4((r << 8) | (lane * VEC + j), wv[j],
-                                                        __float_as_int(pre[j].g), __float_as_int(cp[j]));
-                                outs[j].word = wv[j];      // placeholders, rewritten later
-                                outs[j].wval = 0.0f;
-                                outs[j].abs_eff = 0;
-                                outs[j].coh = pre[j].coh;
-                                outs[j].coh_pre = cp[j];
-                            } else {
-                                outs[j] = step_adamw<FL>(A.P, wv[j], pre[j].g, re, ce[j], vr, vc[j], cp[j], S, pos);
-                            }
-                        }
-                    }
-                } else {
-                    crmath::cr_pow2log2<VEC>(xs, A.P.precond_p, den);
-#pragma unroll
-                    for (int j = 0; j < VEC; ++j) den[j] = pre[j].g / den[j];
-#pragma unroll
-                    for (int j = 0; j < VEC; ++j)
-                        outs[j] = adamw_post<FL, true>(A.P, pre[j], den[j], S, posn ^ (int32_t)(k0 + j));
-                }
+                for (int j = 0; j < VEC; ++j)
+                    outs[j] = adamw_post<FL, true>(A.P, pre[j], den[j], S, posn ^ (int32_t)(k0 + j));
             } else {
 #pragma unroll
                 for (int j = 0; j < VEC; ++j) {
@@ -532,27 +422,6 @@ __global__ void __launch_bounds__(STEP_THREADS, MINB) step_vec_kernel(StepArgs A
         if (track) {
             int m = warp_max(rml);
             if (lane == 0 && m > 0) atomicMax(A.row_max + n, m);
-        }
-    }
-    if (FAST && KIND == CONCORD_KIND_ADAMW) {
-        // elements whose first tick the fast bound could not decide: exact path
-        __syncthreads();
-        const int nd = min(s_ndef, DEF_CAP);
-        for (int i = threadIdx.x; i < nd; i += STEP_THREADS) {
-            const int4 d = s_def[i];
-            const int64_t n = rbase + (d.x >> 8);
-            const int64_t k = (int64_t)blockIdx.x * STEP_COLS + (d.x & 0xff);
-            const int32_t pos = shl32((int32_t)(A.row0 + n), 16) ^ (int32_t)k;
-            const ElemOut o = step_adamw<FL>(A.P, d.y, __int_as_float(d.z), A.row_exp[n], A.col_exp[k],
-                                             need_vhat ? A.v_row[n] : 0.0f, need_vhat ? A.v_col[k] : 0.0f,
-                                             __int_as_float(d.w), S, pos);
-            A.packed[n * A.ldp + k] = o.word;
-            A.wbuf[n * A.ldw + k] = __bfloat16_as_ushort(__float2bfloat16_rn(o.wval));
-            if (write_cp) A.coh_pre[n * A.ldc + k] = o.coh_pre;
-            if (track && o.abs_eff > 0) {
-                atomicMax(A.row_max + n, o.abs_eff);
-                atomicMax(A.col_max + k, o.abs_eff);
-            }
         }
     }
     if (track) {
@@ -605,15 +474,13 @@ __global__ void __launch_bounds__(STEP_THREADS) step_generic_kernel(StepArgs A) 
     if (need_coh && A.coh_stats) block_add_coh(csum, ccnt, A.coh_stats);
 }
 
-template <int MINB, bool FAST>
+template <int MINB>
 static void launch_vec(bool adamw, uint32_t F, bool has_cp, dim3 grid, cudaStream_t s, const StepArgs& A) {
     const bool zero_wd = A.P.wd_sv == 0.0f && A.P.wd_sf == 0.0f;
-    if (!adamw) step_vec_kernel<CONCORD_KIND_SGD, FL_DYNAMIC, MINB, false><<<grid, STEP_THREADS, 0, s>>>(A);
-    else if (F == (FL_BARE & 0xffffu) && has_cp && zero_wd)
-        step_vec_kernel<CONCORD_KIND_ADAMW, FL_BARE, MINB, FAST><<<grid, STEP_THREADS, 0, s>>>(A);
-    else if (F == (FL_NOCOHPRE & 0xffffu) && zero_wd)
-        step_vec_kernel<CONCORD_KIND_ADAMW, FL_NOCOHPRE, MINB, FAST><<<grid, STEP_THREADS, 0, s>>>(A);
-    else step_vec_kernel<CONCORD_KIND_ADAMW, FL_DYNAMIC, MINB, FAST><<<grid, STEP_THREADS, 0, s>>>(A);
+    if (!adamw) step_vec_kernel<CONCORD_KIND_SGD, FL_DYNAMIC, MINB><<<grid, STEP_THREADS, 0, s>>>(A);
+    else if (F == (FL_BARE & 0xffffu) && has_cp && zero_wd) step_vec_kernel<CONCORD_KIND_ADAMW, FL_BARE, MINB><<<grid, STEP_THREADS, 0, s>>>(A);
+    else if (F == (FL_NOCOHPRE & 0xffffu) && zero_wd) step_vec_kernel<CONCORD_KIND_ADAMW, FL_NOCOHPRE, MINB><<<grid, STEP_THREADS, 0, s>>>(A);
+    else step_vec_kernel<CONCORD_KIND_ADAMW, FL_DYNAMIC, MINB><<<grid, STEP_THREADS, 0, s>>>(A);
 }
 
 }  // namespace concord
@@ -660,19 +527,8 @@ extern "C" int concord_step(const concord_step_params* p, int32_t* packed, int64
             const char* e = getenv("CONCORD_STEP_MINB");
             return (e && e[0] == '3') ? 3 : 2;
         }();
-        // bounded fast first tick (default) or the correctly rounded denominator
-        // for every element (CONCORD_STEP_EXACT_POW=1); both give the same words
-        static const bool exact_pow = [] {
-            const char* e = getenv("CONCORD_STEP_EXACT_POW");
-            return e && e[0] == '1';
-        }();
-        if (exact_pow) {
-            if (minb == 2) launch_vec<2, false>(adamw, F, coh_pre != nullptr, grid, s, A);
-            else launch_vec<3, false>(adamw, F, coh_pre != nullptr, grid, s, A);
-        } else {
-            if (minb == 2) launch_vec<2, true>(adamw, F, coh_pre != nullptr, grid, s, A);
-            else launch_vec<3, true>(adamw, F, coh_pre != nullptr, grid, s, A);
-        }
+        if (minb == 2) launch_vec<2>(adamw, F, coh_pre != nullptr, grid, s, A);
+        else launch_vec<3>(adamw, F, coh_pre != nullptr, grid, s, A);
     } else {
         int64_t blocks = (N * K + STEP_THREADS - 1) / STEP_THREADS;
         if (blocks > 148 * 64) blocks = 148 * 64;

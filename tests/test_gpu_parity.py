@@ -243,11 +243,9 @@ def test_coherence_meter(pb, oracle_mod):
 
 
 @pytest.mark.parametrize("lr", [5e-5, 0.05, 2.0])
-def test_step_fast_tick_deferral_paths(pb, oracle_mod, lr):
-    """The step kernel decides most first ticks from a bounded fast denominator
-    and recomputes the undecided elements exactly; a large lr makes |delta_t|
-    large, so many (or, at lr=2, most) elements take the deferred or the
-    list-overflow path.  Words must stay bit-exact whatever the split."""
+def test_step_across_lr_scales(pb, oracle_mod, lr):
+    """From tiny to huge |delta_t| (lr 5e-5 .. 2): SR ticks of every size and
+    the step clamp must stay bit-exact."""
     rng = np.random.default_rng(int(lr * 1e5) + 7)
     N, K = 300, 512
     z = load("step_bare")
