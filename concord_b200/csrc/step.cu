@@ -36,8 +36,13 @@ struct ElemOut {
 constexpr uint32_t FL_DYNAMIC = 0x80000000u;
 // set in an instantiation's flag word: wd_sv == wd_sf == 0 (checked at launch)
 constexpr uint32_t FL_ZERO_WD = 0x40000000u;
+// set in an instantiation's flag word: weight_decay == beta1 == v_scale == 0 and
+// gf_trust_delta_sq == gate_gain == 1 (the bare defaults; checked at launch).
+// With the exponent range of a SAFE row (|te| <= 46, so every product below is
+// finite) the terms they scale are exact no-ops for the ticks.
+constexpr uint32_t FL_PLAIN = 0x20000000u;
 constexpr uint32_t FL_BARE = CONCORD_F_MASS_PRESERVE | CONCORD_F_APPLY_CHASE | CONCORD_F_TRACK_REBALANCE |
-                             CONCORD_F_GF_TRUST | CONCORD_F_COHPRE | CONCORD_F_FIXED_COH | FL_ZERO_WD;
+                             CONCORD_F_GF_TRUST | CONCORD_F_COHPRE | CONCORD_F_FIXED_COH | FL_ZERO_WD | FL_PLAIN;
 constexpr uint32_t FL_NOCOHPRE = FL_BARE & ~CONCORD_F_COHPRE;
 
 template <uint32_t FL>
@@ -76,12 +81,16 @@ __device__ __forceinline__ AdamwPre adamw_pre(const concord_step_params& P, int3
     const float d_sv = (float)(e.s_slow * 128 - e.v_slow * 128);
     const float noise = e.d_fs - P.drift_cancel_C * d_sv;
     const float noise_in_w = noise * scale_fwd;
-    float v_proxy = noise_in_w * noise_in_w * P.v_scale;
+    const bool plain = SAFE && (FL & FL_PLAIN);
+    // v_scale == 0: noise_in_w^2 * 0 == +0 (finite for SAFE rows)
+    float v_proxy = plain ? 0.0f : noise_in_w * noise_in_w * P.v_scale;
     const bool need_vhat = (F & (CONCORD_F_GF_TRUST | CONCORD_F_GF_CONSOL | CONCORD_F_COHPRE | CONCORD_F_RATIO_COH)) != 0;
     const bool need_coh = (F & (CONCORD_F_GF_CONSOL | CONCORD_F_COHPRE | CONCORD_F_RATIO_COH)) != 0;
     float v_hat = 0.0f, coh = 0.0f;
     if (need_vhat) v_hat = v_row * v_col * S.svi;
-    if (F & CONCORD_F_GF_TRUST) v_proxy = v_proxy + P.gf_trust_delta_sq * v_hat;
+    // delta_sq == 1 and v_hat >= +0: 0 + 1 * v_hat == v_hat
+    if (plain) v_proxy = v_hat;
+    else if (F & CONCORD_F_GF_TRUST) v_proxy = v_proxy + P.gf_trust_delta_sq * v_hat;
     if (need_coh) {
         if (F & CONCORD_F_FIXED_COH) {
             const float sig_w = P.drift_cancel_C * d_sv * scale_fwd;
@@ -142,7 +151,8 @@ __device__ __forceinline__ ElemOut adamw_post(const concord_step_params& P, cons
         } else if (F & CONCORD_F_COHPRE) {
             const float gate = coh + e.cp * (1.0f - coh);
             cp_new = P.one_minus_alpha_v_fast * e.cp + P.alpha_v_fast * coh;
-            chase_mantissa = P.alpha * gate * P.gate_gain * (float)s_fast;
+            chase_mantissa = (SAFE && (FL & FL_PLAIN)) ? P.alpha * gate * (float)s_fast   // gate_gain == 1
+                                                       : P.alpha * gate * P.gate_gain * (float)s_fast;
         } else {
             chase_mantissa = P.alpha_gate_gain * (float)s_fast;
         }
@@ -328,7 +338,7 @@ __global__ void __launch_bounds__(STEP_THREADS, MINB) step_vec_kernel(StepArgs A
     }
     bool cols_safe = true;
 #pragma unroll
-    for (int j = 0; j < VEC; ++j) cols_safe &= (uint32_t)(ce[j] + 63) <= 126u;
+    for (int j = 0; j < VEC; ++j) cols_safe &= (uint32_t)(ce[j] + 23) <= 46u;
     float csum = 0.0f;
     int ccnt = 0;
     // rows of this warp: rbase + warp + 8 i; the next row's inputs are loaded
@@ -367,7 +377,8 @@ __global__ void __launch_bounds__(STEP_THREADS, MINB) step_vec_kernel(StepArgs A
             float wf[VEC];
             const int32_t posn = shl32((int32_t)(A.row0 + n), 16);
             ElemOut outs[VEC];
-            const bool safe = cols_safe && (uint32_t)(re - A.P.mantissa_bias + 63) <= 126u;
+            // SAFE rows: |te| <= 46, so 2^te and the products it scales stay finite
+            const bool safe = cols_safe && (uint32_t)(re - A.P.mantissa_bias + 23) <= 46u;
             if (KIND == CONCORD_KIND_ADAMW && !safe) {
 #pragma unroll
                 for (int j = 0; j < VEC; ++j) {
@@ -476,7 +487,9 @@ __global__ void __launch_bounds__(STEP_THREADS) step_generic_kernel(StepArgs A) 
 
 template <int MINB>
 static void launch_vec(bool adamw, uint32_t F, bool has_cp, dim3 grid, cudaStream_t s, const StepArgs& A) {
-    const bool zero_wd = A.P.wd_sv == 0.0f && A.P.wd_sf == 0.0f;
+    const bool zero_wd = A.P.wd_sv == 0.0f && A.P.wd_sf == 0.0f && A.P.weight_decay == 0.0f &&
+                         A.P.beta1 == 0.0f && A.P.v_scale == 0.0f && A.P.gf_trust_delta_sq == 1.0f &&
+                         A.P.gate_gain == 1.0f && fabsf(A.P.drift_cancel_C) <= 1.0f;
     if (!adamw) step_vec_kernel<CONCORD_KIND_SGD, FL_DYNAMIC, MINB><<<grid, STEP_THREADS, 0, s>>>(A);
     else if (F == (FL_BARE & 0xffffu) && has_cp && zero_wd) step_vec_kernel<CONCORD_KIND_ADAMW, FL_BARE, MINB><<<grid, STEP_THREADS, 0, s>>>(A);
     else if (F == (FL_NOCOHPRE & 0xffffu) && zero_wd) step_vec_kernel<CONCORD_KIND_ADAMW, FL_NOCOHPRE, MINB><<<grid, STEP_THREADS, 0, s>>>(A);
