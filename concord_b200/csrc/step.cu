@@ -191,6 +191,90 @@ __device__ __forceinline__ ElemOut adamw_post(const concord_step_params& P, cons
     return o;
 }
 
+// adamw_post for W elements in lockstep: every stage runs for all W elements
+// before the next one, so the W dependent chains (three SR ticks each) sit
+// side by side for the scheduler.  Same arithmetic as adamw_post.
+template <uint32_t FL, int W>
+__device__ __forceinline__ void adamw_post_lockstep(const concord_step_params& P, const AdamwPre (&e)[W],
+                                                    const float (&step_div)[W], const StepScalars& S,
+                                                    const int32_t (&pos)[W], ElemOut (&o)[W]) {
+    const uint32_t F = flags_of<FL>(P);
+    const bool plain = (FL & FL_PLAIN) != 0;
+    const bool consol = (F & CONCORD_F_GF_CONSOL) != 0;
+    int32_t sf[W], ss[W], nv[W];
+    float cpn[W];
+#pragma unroll
+    for (int j = 0; j < W; ++j) {
+        const float scale_fwd = pow2_exp<true>(e[j].te), scale_inv = pow2_exp<true>(-e[j].te);
+        float step_live = clamp_np(step_div[j], P.step_cap);
+        float evap = 0.0f;
+        if (consol) evap = S.lr * P.gf_consol * (1.0f - e[j].coh) * e[j].d_fs;
+        else if (!plain) step_live = step_live + P.weight_decay * (e[j].d_fs * scale_fwd);
+        float delta_t = -S.lr * step_live * scale_inv;
+        if (!plain) delta_t = delta_t - P.beta1 * e[j].d_fs;
+        if (consol) delta_t = delta_t - evap;
+        sf[j] = e[j].s_fast + sr_tick(delta_t, hash_uniform(e[j].s_fast, pos[j], S.salt));
+        ss[j] = e[j].s_slow;
+        nv[j] = e[j].v_slow;
+        cpn[j] = e[j].cp;
+    }
+    if (F & CONCORD_F_APPLY_CHASE) {
+#pragma unroll
+        for (int j = 0; j < W; ++j) {
+            const float coh = e[j].coh;
+            float chase_mantissa;
+            if (F & CONCORD_F_RATIO_COH) {
+                const float gate = P.chase_floor + P.one_minus_chase_floor * coh;
+                chase_mantissa = P.alpha * gate * P.gate_gain * (float)sf[j];
+            } else if (F & CONCORD_F_COHPRE) {
+                const float gate = coh + e[j].cp * (1.0f - coh);
+                cpn[j] = P.one_minus_alpha_v_fast * e[j].cp + P.alpha_v_fast * coh;
+                chase_mantissa = plain ? P.alpha * gate * (float)sf[j] : P.alpha * gate * P.gate_gain * (float)sf[j];
+            } else {
+                chase_mantissa = P.alpha_gate_gain * (float)sf[j];
+            }
+            const int32_t ts = sr_tick(chase_mantissa / 128.0f, hash_uniform(sf[j], pos[j], S.salt ^ 0x5A5A5A5A));
+            ss[j] = ss[j] + ts;
+            sf[j] = sf[j] - ts * 128;
+        }
+#pragma unroll
+        for (int j = 0; j < W; ++j) {
+            const int32_t v_slow = e[j].v_slow;
+            float delta_v8 = P.alpha_v_fast * (float)(ss[j] * 128 - v_slow * 128) / 128.0f;
+            if (F & CONCORD_F_RATIO_COH)
+                delta_v8 = delta_v8 * (P.leak_floor + P.one_minus_leak_floor * e[j].coh);
+            const int32_t tv = sr_tick(delta_v8, hash_uniform(sf[j], pos[j], S.salt ^ 0x33335555));
+            nv[j] = clampi(v_slow + tv, -128, 127);
+            if (F & CONCORD_F_MASS_PRESERVE) ss[j] = ss[j] - (nv[j] - v_slow);
+        }
+        if (!(FL & FL_ZERO_WD)) {
+#pragma unroll
+            for (int j = 0; j < W; ++j) {
+                const int32_t v_full_post = nv[j] * 128;
+                if (P.wd_sv != 0.0f) {
+                    const float d = S.lr * P.wd_sv * (float)(ss[j] * 128 - v_full_post) / 128.0f;
+                    ss[j] = ss[j] - sr_tick(d, hash_uniform(sf[j], pos[j], S.salt ^ 0x66665555));
+                }
+                if (P.wd_sf != 0.0f) {
+                    const float d = S.lr * P.wd_sf * (float)(ss[j] * 128 + sf[j] - v_full_post);
+                    sf[j] = sf[j] - sr_tick(d, hash_uniform(sf[j], pos[j], S.salt ^ 0x77770000));
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < W; ++j) {
+        const int32_t sfc = clampi(sf[j], -32768, 32767);
+        const int32_t ssc = clampi(ss[j], -128, 127);
+        const int32_t m_new = ssc * 128 + sfc + nv[j] * 128;
+        o[j].word = repack(sfc, ssc, nv[j]);
+        o[j].wval = (float)m_new * pow2_exp<true>(e[j].te);
+        o[j].abs_eff = abs(m_new);
+        o[j].coh = e[j].coh;
+        o[j].coh_pre = cpn[j];
+    }
+}
+
 // One element of the AdamW-path step (packed_b.py:476-703).
 template <uint32_t FL>
 __device__ __forceinline__ ElemOut step_adamw(const concord_step_params& P, int32_t packed, float g,
@@ -402,9 +486,10 @@ __global__ void __launch_bounds__(STEP_THREADS, MINB) step_vec_kernel(StepArgs A
                 crmath::cr_pow2log2<VEC>(xs, A.P.precond_p, den);
 #pragma unroll
                 for (int j = 0; j < VEC; ++j) den[j] = pre[j].g / den[j];
+                int32_t posv[VEC];
 #pragma unroll
-                for (int j = 0; j < VEC; ++j)
-                    outs[j] = adamw_post<FL, true>(A.P, pre[j], den[j], S, posn ^ (int32_t)(k0 + j));
+                for (int j = 0; j < VEC; ++j) posv[j] = posn ^ (int32_t)(k0 + j);
+                adamw_post_lockstep<FL, VEC>(A.P, pre, den, S, posv, outs);
             } else {
 #pragma unroll
                 for (int j = 0; j < VEC; ++j) {
