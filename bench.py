@@ -162,7 +162,33 @@ def bench_ours(args, rank, world, device):
     for i in range(args.warmup):
         optimizer_step(layer, grads[i % 2])
     torch.cuda.synchronize()
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    # kernel timing pass (eager, CUDA events around the v-hat and step launches)
+    n_ev = min(args.steps, 200)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(n_ev)]
+    for i in range(n_ev):
+        optimizer_step(layer, grads[i % 2], ev=evs[i])
+    torch.cuda.synchronize()
+    step_kernel_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    vhat_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    # the timed pass replays the step as CUDA graphs (one per gradient buffer):
+    # the optimizer path has no host synchronisation, so it captures whole
+    graphs = None
+    if args.graph:
+        try:
+            graphs = []
+            for gbuf in grads:
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr):
+                    optimizer_step(layer, gbuf)
+                graphs.append(gr)
+            for i in range(2):
+                graphs[i % 2].replay()
+            torch.cuda.synchronize()
+        except Exception as ex:  # noqa: BLE001 - report and time eagerly
+            print(f"[bench] graph capture unavailable ({type(ex).__name__}: {ex}); timing eagerly",
+                  file=sys.stderr)
+            graphs = None
+            torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -172,15 +198,16 @@ def bench_ours(args, rank, world, device):
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
     for i in range(args.steps):
-        optimizer_step(layer, grads[i % 2], ev=evs[i])
+        if graphs is not None:
+            graphs[i % 2].replay()
+        else:
+            optimizer_step(layer, grads[i % 2])
     t1.record()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     clk = clocks.stop()
     ms = t0.elapsed_time(t1) / args.steps
-    step_kernel_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
-    vhat_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
     # end to end through the public API: grad from pinned host memory every
     # step, the coherence meter read back every step
     host_grads = [g.cpu().pin_memory() for g in grads]
@@ -207,7 +234,7 @@ def bench_ours(args, rank, world, device):
     ms, e2e_ms, step_kernel_ms = t.tolist()
     return dict(ms=ms, e2e_ms=e2e_ms, step_kernel_ms=step_kernel_ms, vhat_ms=vhat_ms,
                 bytes_step=bytes_step, params=params, gemm_ms=gemm_ms, clocks=clk,
-                h2d=grads[0].numel() * 2, d2h=16)
+                h2d=grads[0].numel() * 2, d2h=16, graphs=graphs is not None)
 
 
 def oracle_sample(rows, k_cols, seed=3):
@@ -281,6 +308,8 @@ def main():
     ap.add_argument("--rows", type=int, default=N)
     ap.add_argument("--cols", type=int, default=K)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", dest="graph", action="store_false",
+                    help="time eager launches instead of CUDA-graph replays")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -333,6 +362,7 @@ def main():
                      "algorithmic_bytes_per_launch": shard_params * STEP_BYTES_PER_PARAM,
                      "kernel_ms": r["step_kernel_ms"]},
         "vhat_ms": r["vhat_ms"],
+        "cuda_graph": r["graphs"],
         "gemm": {k: {"ms": v, "tflops": flops / (v * 1e-3) / 1e12} for k, v in r["gemm_ms"].items()},
         "gemm_impl": "fwd/dx/dw: concord tcgen05 kernels (CUTLASS sm100 templates); cublas_*: torch",
         "clocks": r["clocks"],

@@ -61,13 +61,24 @@ __global__ void __launch_bounds__(VH_THREADS) vhat_kernel(VhatArgs A) {
     float cacc[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) cacc[j] = 0.0f;
+    // issue all of this warp's row loads before any arithmetic (vector path)
+    uint4 raw[VH_ROWS / 8];
+    if (A.vec && k0 < A.K) {
+#pragma unroll
+        for (int i = 0; i < VH_ROWS / 8; ++i) {
+            const int64_t n = (int64_t)rb * VH_ROWS + warp + 8 * i;
+            raw[i] = n < A.N ? __ldcs(reinterpret_cast<const uint4*>(A.grad + n * A.ldg + k0))
+                             : make_uint4(0, 0, 0, 0);
+        }
+    }
+#pragma unroll
     for (int i = 0; i < VH_ROWS / 8; ++i) {
         const int64_t n = (int64_t)rb * VH_ROWS + warp + 8 * i;
         float g2[8];
         if (n < A.N) {
             const uint16_t* gp = A.grad + n * A.ldg + k0;
             if (A.vec && k0 < A.K) {
-                uint4 v = __ldg(reinterpret_cast<const uint4*>(gp));
+                const uint4 v = raw[i];
                 uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
