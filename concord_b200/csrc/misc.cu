@@ -71,6 +71,31 @@ __global__ void quantize_kernel(const float* W, int64_t ldw, int32_t* packed, in
     }
 }
 
+// vector form: 4 consecutive columns per thread, a 2-D grid (no 64-bit division)
+__global__ void materialize_vec_kernel(const int32_t* packed, int64_t ldp, const int8_t* row_exp,
+                                       const int8_t* col_exp, uint16_t* out, int64_t ldo, int64_t N,
+                                       int64_t K, int32_t mb, int32_t consolidated) {
+    const int64_t k0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (k0 >= K) return;
+    const uint32_t c4 = *reinterpret_cast<const uint32_t*>(col_exp + k0);
+    for (int64_t n = blockIdx.y; n < N; n += gridDim.y) {
+        const int4 w = __ldcs(reinterpret_cast<const int4*>(packed + n * ldp + k0));
+        const int32_t re = row_exp[n] - mb;
+        const int32_t wv[4] = {w.x, w.y, w.z, w.w};
+        float f[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int32_t v = wv[j];
+            const int32_t sf = v >> 16, ss = shl32(v, 16) >> 24, vs = shl32(v, 24) >> 24;
+            const int32_t m = consolidated ? ss * 128 + vs * 128 : ss * 128 + sf + vs * 128;
+            f[j] = (float)m * exp2i(re + (int32_t)(int8_t)(c4 >> (8 * j)));
+        }
+        const uint32_t lo = (uint32_t)f32_to_bf16(f[0]) | ((uint32_t)f32_to_bf16(f[1]) << 16);
+        const uint32_t hi = (uint32_t)f32_to_bf16(f[2]) | ((uint32_t)f32_to_bf16(f[3]) << 16);
+        __stcs(reinterpret_cast<uint2*>(out + n * ldo + k0), make_uint2(lo, hi));
+    }
+}
+
 __global__ void zero_i8_kernel(int8_t* p, int64_t n) {
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) p[i] = 0;
 }
@@ -132,8 +157,15 @@ extern "C" int concord_materialize(const int32_t* packed, int64_t ldp, const int
     if (!packed || !row_exp || !col_exp || !out) return fail(CONCORD_EINVAL, "concord_materialize: null pointer");
     if (N < 0 || K < 0 || ldp < K || ldo < K) return fail(CONCORD_ESHAPE, "concord_materialize: bad shape/stride");
     if (N == 0 || K == 0) return CONCORD_OK;
-    materialize_kernel<<<grid_for(N * K, 256), 256, 0, as_stream(stream)>>>(packed, ldp, row_exp, col_exp, out, ldo, N, K,
-                                                                          mantissa_bias, consolidated);
+    if (K % 4 == 0 && ldp % 4 == 0 && ldo % 4 == 0 && aligned(packed, 16) && aligned(out, 8) && aligned(col_exp, 4)) {
+        const int64_t tx = (K / 4 + 127) / 128;
+        int64_t ty = N < 4096 ? N : 4096;
+        materialize_vec_kernel<<<dim3((unsigned)tx, (unsigned)ty), 128, 0, as_stream(stream)>>>(
+            packed, ldp, row_exp, col_exp, out, ldo, N, K, mantissa_bias, consolidated);
+    } else {
+        materialize_kernel<<<grid_for(N * K, 256), 256, 0, as_stream(stream)>>>(packed, ldp, row_exp, col_exp, out,
+                                                                              ldo, N, K, mantissa_bias, consolidated);
+    }
     return check_launch("concord_materialize");
 }
 

@@ -12,9 +12,10 @@ the step salt, lr) -- so the optimizer half of the backward shards by rows:
      sum_v_inv finished identically on every rank;
   3. the fused packed step on the shard, with global row offsets (the SR
      hash position uses the global row) and the same salt on every rank;
-  4. all-reduce(max) of the column maxima, all-gather of the row maxima, of
-     the packed words (4 B/param) and of v_row; every rank re-derives the
-     bf16 forward weight from the gathered words (what the step emitted).
+  4. all-reduce(max) of the column maxima, one all-gather of (row maxima,
+     v_row), one all-gather of the packed words (4 B/param, in place when N
+     divides evenly); every rank re-derives the bf16 forward weight from the
+     gathered words (what the step emitted).
 rebalance() then runs replicated on identical inputs, so exponents, seeds and
 words stay identical on every rank with no further traffic.
 
@@ -107,13 +108,13 @@ class RowShardedStep:
         self.grad_pad = torch.zeros(pad, K, dtype=torch.bfloat16, device=dev)
         self.grad_shard = torch.empty(self.S, K, dtype=torch.bfloat16, device=dev)
         self.words_pad = torch.zeros(pad, K, dtype=torch.int32, device=dev)
-        self.vrow_pad = torch.zeros(pad, dtype=torch.float32, device=dev)
-        self.rmax_pad = torch.zeros(pad, dtype=torch.int32, device=dev)
         self.red = torch.zeros(K + 1, dtype=torch.float32, device=dev)
         self.wshard = torch.empty(self.S, K, dtype=torch.bfloat16, device=dev)
         self.loc_w = torch.zeros(self.S, K, dtype=torch.int32, device=dev)
-        self.loc_r = torch.zeros(self.S, dtype=torch.int32, device=dev)
-        self.loc_v = torch.zeros(self.S, dtype=torch.float32, device=dev)
+        # row maxima and v_row of the shard travel together in one all-gather
+        self.loc_rv = torch.zeros(2, self.S, dtype=torch.int32, device=dev)
+        self.all_rv = torch.zeros(self.P, 2, self.S, dtype=torch.int32, device=dev)
+        self.even = (N == pad)   # no padding: collectives work in place on the layer's tensors
         self.step_events = None   # optional [_, start, end] CUDA events around the shard's step
 
     @torch.no_grad()
@@ -123,8 +124,11 @@ class RowShardedStep:
         n_loc = r1 - r0
         wbuf, rmax, cmax = L._ensure_buffers()
         # 1. reduce-scatter of the bf16 gradient over rows
-        self.grad_pad[:N].copy_(grad_local)
-        _reduce_scatter(self.grad_shard, self.grad_pad, g)
+        if self.even and grad_local.is_contiguous():
+            _reduce_scatter(self.grad_shard, grad_local, g)
+        else:
+            self.grad_pad[:N].copy_(grad_local)
+            _reduce_scatter(self.grad_shard, self.grad_pad, g)
         gs = self.grad_shard[:n_loc]
         # 2. v-hat: shard partials, one all-reduce, replicated finish
         track = bool(L.track_rebalance)
@@ -161,13 +165,16 @@ class RowShardedStep:
         # 4. maxima, words and v_row back to every rank; forward weight re-derived
         if track:
             dist.all_reduce(cmax, op=dist.ReduceOp.MAX, group=g)
-            self.loc_r[:n_loc].copy_(rmax[r0:r1])
-            _all_gather(self.rmax_pad, self.loc_r, g)
-            rmax.copy_(self.rmax_pad[:N])
-        self.loc_w[:n_loc].copy_(L.packed_w[r0:r1])
-        _all_gather(self.words_pad, self.loc_w, g)
-        L.packed_w.copy_(self.words_pad[:N])
-        self.loc_v[:n_loc].copy_(L.v_row[r0:r1])
-        _all_gather(self.vrow_pad, self.loc_v, g)
-        L.v_row.copy_(self.vrow_pad[:N])
+        self.loc_rv[0, :n_loc].copy_(rmax[r0:r1])
+        self.loc_rv[1, :n_loc].copy_(L.v_row[r0:r1].view(torch.int32))
+        _all_gather(self.all_rv, self.loc_rv, g)
+        if track:
+            rmax.copy_(self.all_rv[:, 0].reshape(-1)[:N])
+        L.v_row.copy_(self.all_rv[:, 1].reshape(-1)[:N].view(torch.float32))
+        if self.even:
+            _all_gather(L.packed_w, L.packed_w[r0:r1], g)     # in place
+        else:
+            self.loc_w[:n_loc].copy_(L.packed_w[r0:r1])
+            _all_gather(self.words_pad, self.loc_w, g)
+            L.packed_w.copy_(self.words_pad[:N])
         kern.materialize(L.packed_w, L.row_exp, L.col_exp, wbuf, L.MANTISSA_BIAS)

@@ -16,15 +16,15 @@ import torch.multiprocessing as mp
 
 pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-N, K, STEPS = 301, 512, 4
+K, STEPS = 512, 4
 
 
-def _grad(step, rank, dev):
+def _grad(N, step, rank, dev):
     g = torch.Generator(device="cpu").manual_seed(1000 * step + rank)
     return (torch.randn(N, K, generator=g) * 3e-2).to(torch.bfloat16).to(dev)
 
 
-def _layer(dev):
+def _layer(N, dev):
     from concord_b200 import ConcordLinearPackedB
     torch.manual_seed(5)
     layer = ConcordLinearPackedB(K, N, bias=False, device=dev, lr=0.05)
@@ -41,7 +41,7 @@ def _state(layer):
     return out
 
 
-def _worker(rank, world, port, out_dir):
+def _worker(rank, world, port, out_dir, N):
     import sys
     sys.path.insert(0, ROOT)
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -49,10 +49,10 @@ def _worker(rank, world, port, out_dir):
     dist.init_process_group("nccl", rank=rank, world_size=world)
     from concord_b200.distributed import RowShardedStep
     dev = torch.device("cuda", rank)
-    layer = _layer(dev)
+    layer = _layer(N, dev)
     st = RowShardedStep(layer)
     for s in range(STEPS):
-        st.step(_grad(s, rank, dev))
+        st.step(_grad(N, s, rank, dev))
         layer.rebalance()
     torch.cuda.synchronize()
     np.savez(os.path.join(out_dir, f"rank{rank}.npz"), **_state(layer))
@@ -60,20 +60,20 @@ def _worker(rank, world, port, out_dir):
     dist.destroy_process_group()
 
 
-def _emulate(world):
+def _emulate(world, N):
     """The same sharded arithmetic on one GPU, shard by shard."""
     from concord_b200 import packed_b as pb
     from concord_b200.distributed import CudaKernels as KK
     dev = torch.device("cuda", 0)
-    L = _layer(dev)
+    L = _layer(N, dev)
     S = (N + world - 1) // world
     wbuf, rmax, cmax = L._ensure_buffers()
     red = torch.zeros(K + 1, dtype=torch.float32, device=dev)
     salt = pb._get_step_counter(dev)
     for s in range(STEPS):
-        tot = _grad(s, 0, dev).float()
+        tot = _grad(N, s, 0, dev).float()
         for r in range(1, world):
-            tot = tot + _grad(s, r, dev).float()
+            tot = tot + _grad(N, s, r, dev).float()
         g = tot.to(torch.bfloat16)
         acc = torch.zeros(K + 1, dtype=torch.float32, device=dev)
         for r in range(world):
@@ -109,12 +109,13 @@ def _free_port():
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_row_sharded_step_two_gpus(tmp_path):
+@pytest.mark.parametrize("N", [300, 301])   # even split (in-place collectives) and padded
+def test_row_sharded_step_two_gpus(tmp_path, N):
     world = 2
-    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path), N), nprocs=world,
                        join=True, start_method="spawn")
     r = [dict(np.load(tmp_path / f"rank{i}.npz")) for i in range(world)]
-    ref = _emulate(world)
+    ref = _emulate(world, N)
     for key in ref:
         np.testing.assert_array_equal(r[0][key], r[1][key], err_msg=key)
         np.testing.assert_array_equal(r[0][key], ref[key], err_msg=key)
