@@ -70,6 +70,7 @@ def _emulate(world, N):
     wbuf, rmax, cmax = L._ensure_buffers()
     red = torch.zeros(K + 1, dtype=torch.float32, device=dev)
     salt = pb._get_step_counter(dev)
+    salt.zero_()          # the workers' counters start at 0 in fresh processes
     for s in range(STEPS):
         tot = _grad(N, s, 0, dev).float()
         for r in range(1, world):
