@@ -144,9 +144,10 @@ def optimizer_step(layer, grad, coh_stats=None, ev=None):
     if SHARDED is not None:
         SHARDED.step_events = ev
         SHARDED.step(grad)
+        SHARDED.rebalance()
     else:
         layer.optimizer_step(grad, coh_stats=coh_stats, step_events=ev)
-    layer.rebalance()
+        layer.rebalance()
 
 
 def bench_ours(args, rank, world, device):
@@ -295,8 +296,9 @@ def base_line(args, world):
                                    f"(M={M}, K={args.cols}, N={args.rows}); bare-default ConcordLinearPackedB",
                        "M": M, "K": args.cols, "N": args.rows, "params": args.rows * args.cols,
                        "l2_flush": "not needed: working set > 126 MB L2",
-                       "parallelism": (f"dp{world}: row-sharded packed step (NCCL reduce-scatter bf16 dW, "
-                                       "all-gather int32 words)") if world > 1 else "single"}}
+                       "parallelism": (f"dp{world}: row-sharded packed step and state (NCCL reduce-scatter of "
+                                       "bf16 dW, all-gather of the bf16 forward weight)")
+                                      if world > 1 else "single"}}
 
 
 def main():

@@ -57,6 +57,13 @@ class OracleKernels:
                     row_max.numpy(), col_max.numpy(), v_row.numpy(), v_col.numpy(),
                     sum_v_inv.numpy(), None if coh_pre is None else coh_pre.numpy(),
                     float(lr_t[0]), float(eps_t[0]), int(salt[0]), row0=row0)
+        wbuf.copy_(torch.from_numpy(w.view(np.int16)).view(torch.bfloat16))
+
+    def rebalance(self, packed, row_exp, col_exp, row_max, col_max, row_hwm, col_hwm, seed, max_m,
+                  exp_max, exp_min, row0, n_total, fired_out=None):
+        self.o.rebalance(packed.numpy(), row_exp.numpy(), col_exp.numpy(), row_max.numpy(),
+                         col_max.numpy(), row_hwm.numpy(), col_hwm.numpy(), seed.numpy(), max_m,
+                         exp_max, exp_min, row0=row0, n_total=n_total)
 
     def materialize(self, packed, row_exp, col_exp, out, mantissa_bias):
         w = self.o.materialize(packed.numpy(), row_exp.numpy(), col_exp.numpy(), mantissa_bias)
@@ -64,6 +71,11 @@ class OracleKernels:
 
     def salt(self, device):
         return self._salt
+
+
+def make_layer_W(seed=0):
+    rng = np.random.default_rng(seed)
+    return (rng.standard_normal((N, K)) * 0.05).astype(np.float32)
 
 
 def make_layer(seed=0):
@@ -75,15 +87,18 @@ def make_layer(seed=0):
     L = SimpleNamespace(
         packed_w=torch.from_numpy(packed), row_exp=torch.from_numpy(rexp),
         col_exp=torch.from_numpy(cexp), v_row=torch.zeros(N), v_col=torch.zeros(K),
-        _sum_v_inv=torch.ones(1), _coh_pre=torch.ones(N, K), _lr_buf=torch.tensor([0.01]),
+        _sum_v_inv=torch.ones(1), _coh_pre=torch.ones(N, K), _lr_buf=torch.tensor([0.5]),
         _eps_buf=torch.tensor([1e-10]), track_rebalance=True, adafactor_beta2=0.999,
         optimizer_kind='adamw', alpha=0.1, beta1=0.0, weight_decay=0.0, step_cap=10.0,
         v_scale=0.0, precond_p=0.5, gf_consol=0.0,
         drift_cancel_C=compute_drift_cancel_C(0.1, 0.001), alpha_v_fast=0.001, wd_sv=0.0,
         wd_sf=0.0, mass_preserve_v=True, apply_chase=True, gf_trust_delta_sq=1.0,
-        MANTISSA_BIAS=15)
+        MANTISSA_BIAS=15, MAX_M=24000, EXP_MAX=7, EXP_MIN=-8, allow_tickdown=False,
+        _reb_seed=torch.zeros(1, dtype=torch.int32), _row_max_hwm=torch.zeros(N, dtype=torch.int32),
+        _col_max_hwm=torch.zeros(K, dtype=torch.int32))
     bufs = (torch.zeros(N, K, dtype=torch.bfloat16), torch.zeros(N, dtype=torch.int32),
             torch.zeros(K, dtype=torch.int32))
+    L._bf16_weight_buf, L._row_max_buf, L._col_max_buf = bufs
     L._ensure_buffers = lambda: bufs
     return L
 
@@ -104,11 +119,14 @@ def _worker(rank, world, port, out_dir):
     st = RowShardedStep(L, kernels=OracleKernels())
     for s in range(3):
         st.step(grads(s, rank))
+        st.rebalance()
+    st.gather_state()
     wbuf, rmax, cmax = L._ensure_buffers()
     np.savez(os.path.join(out_dir, f"rank{rank}.npz"), packed=L.packed_w.numpy(),
              v_row=L.v_row.numpy(), v_col=L.v_col.numpy(), svi=L._sum_v_inv.numpy(),
-             wbuf=_np_bf16(wbuf), rmax=rmax.numpy(), cmax=cmax.numpy(),
-             coh=L._coh_pre.numpy(), r0=st.r0, r1=st.r1)
+             wbuf=_np_bf16(wbuf), cmax=cmax.numpy(), coh=L._coh_pre.numpy(),
+             row_exp=L.row_exp.numpy(), col_exp=L.col_exp.numpy(), seed=L._reb_seed.numpy(),
+             hwm=L._row_max_hwm.numpy())
     dist.destroy_process_group()
 
 
@@ -123,6 +141,10 @@ def emulate(world):
     svi = np.ones(1, np.float32)
     P = adamw_params(v_scale=0.0, precond_p=0.5, drift_cancel_C=L.drift_cancel_C,
                      mass_preserve=True, gf_trust_delta_sq=1.0, use_cohpre=True)
+    rexp, cexp = L.row_exp.numpy(), L.col_exp.numpy()
+    seed = np.zeros(1, np.int32)
+    hr, hc = np.zeros(N, np.int32), np.zeros(K, np.int32)
+    wbuf = np.zeros((N, K), np.uint16)
     for s in range(3):
         tot = grads(s, 0).float()
         for r in range(1, world):
@@ -140,12 +162,13 @@ def emulate(world):
         for r in range(world):
             r0, r1 = r * S, min(N, r * S + S)
             w = np.zeros((r1 - r0, K), np.uint16)
-            oracle.step(P, packed[r0:r1], np.ascontiguousarray(g[r0:r1]), w, L.row_exp.numpy()[r0:r1],
-                        L.col_exp.numpy(), rmax[r0:r1], cmax, v_row[r0:r1], v_col, svi, coh[r0:r1],
-                        0.01, 1e-10, s + 1, row0=r0)
-    wbuf = oracle.materialize(packed, L.row_exp.numpy(), L.col_exp.numpy())
-    return dict(packed=packed, v_row=v_row, v_col=v_col, svi=svi, wbuf=wbuf, rmax=rmax,
-                cmax=cmax, coh=coh)
+            oracle.step(P, packed[r0:r1], np.ascontiguousarray(g[r0:r1]), w, rexp[r0:r1], cexp,
+                        rmax[r0:r1], cmax, v_row[r0:r1], v_col, svi, coh[r0:r1],
+                        0.5, 1e-10, s + 1, row0=r0)
+            wbuf[r0:r1] = w
+        oracle.rebalance(packed, rexp, cexp, rmax, cmax, hr, hc, seed)
+    return dict(packed=packed, v_row=v_row, v_col=v_col, svi=svi, wbuf=wbuf, cmax=cmax, coh=coh,
+                row_exp=rexp, col_exp=cexp, seed=seed, hwm=hr)
 
 
 def _free_port():
@@ -162,12 +185,12 @@ def test_row_sharded_step_two_ranks(tmp_path, oracle_mod):
                        join=True, start_method="spawn")
     r = [dict(np.load(tmp_path / f"rank{i}.npz")) for i in range(world)]
     ref = emulate(world)
-    for key in ("packed", "v_row", "v_col", "svi", "wbuf", "rmax", "cmax"):
+    for key in ("packed", "v_row", "v_col", "svi", "wbuf", "cmax", "coh", "row_exp", "col_exp",
+                "seed", "hwm"):
         np.testing.assert_array_equal(r[0][key], r[1][key], err_msg=key)
         np.testing.assert_array_equal(r[0][key], ref[key], err_msg=key)
-    for i in range(world):   # coh_pre is current on each rank's own rows
-        a, b = int(r[i]["r0"]), int(r[i]["r1"])
-        np.testing.assert_array_equal(r[i]["coh"][a:b], ref["coh"][a:b])
+    from oracle import oracle
+    assert (r[0]["row_exp"] != oracle.quantize(make_layer_W())[1]).any(), "rebalance never fired"
 
 
 def _failing_worker(rank, world, port, out_dir):

@@ -53,7 +53,8 @@ def _worker(rank, world, port, out_dir, N):
     st = RowShardedStep(layer)
     for s in range(STEPS):
         st.step(_grad(N, s, rank, dev))
-        layer.rebalance()
+        st.rebalance()
+    st.gather_state()
     torch.cuda.synchronize()
     np.savez(os.path.join(out_dir, f"rank{rank}.npz"), **_state(layer))
     dist.barrier()
