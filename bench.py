@@ -229,6 +229,8 @@ def bench_ours(args, rank, world, device):
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / args.steps
+    if SHARDED is not None:
+        SHARDED.check()   # a cross-GPU wait that ran out would have skipped work: no number then
     t = torch.tensor([ms, e2e_ms, step_kernel_ms], device=device)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -296,8 +298,11 @@ def base_line(args, world):
                                    f"(M={M}, K={args.cols}, N={args.rows}); bare-default ConcordLinearPackedB",
                        "M": M, "K": args.cols, "N": args.rows, "params": args.rows * args.cols,
                        "l2_flush": "not needed: working set > 126 MB L2",
-                       "parallelism": (f"dp{world}: row-sharded packed step and state (NCCL reduce-scatter of "
-                                       "bf16 dW, all-gather of the bf16 forward weight)")
+                       "parallelism": (f"dp{world}: row-sharded packed step and state; "
+                                       + (SHARDED.transport if SHARDED is not None else "?") +
+                                       " transport (peer: dW rows pushed over NVLink to their owners, summed with the v-hat pass, "
+                                       "bf16 weight pushed to every rank by the step kernel; "
+                                       "collective: NCCL reduce-scatter / all-gather)")
                                       if world > 1 else "single"}}
 
 
@@ -368,8 +373,11 @@ def main():
         "gemm": {k: {"ms": v, "tflops": flops / (v * 1e-3) / 1e12} for k, v in r["gemm_ms"].items()},
         "gemm_impl": "fwd/dx/dw: concord tcgen05 kernels (CUTLASS sm100 templates); cublas_*: torch",
         "clocks": r["clocks"],
-        "gpu_launches": args.steps * 4,
-        "gpu_launches_note": "per step: vhat 1 + step 1 + rebalance decide 1 + shift 1 (+1 memset node)",
+        "gpu_launches": args.steps * (4 if world == 1 else (6 if SHARDED.peer is not None else 5)),
+        "gpu_launches_note": ("per step: vhat 1 + step 1 + rebalance decide 1 + shift 1 (+1 memset node)"
+                              if world == 1 else
+                              "per step: [peer reduce 1] + vhat partial 1 + finish 1 + step 1 + rebalance 2; "
+                              "plus NCCL collectives (not counted)"),
     })
     if not args.no_cpu_baseline:
         v1, dt = cpu_baseline(rows=2048, threads=1)

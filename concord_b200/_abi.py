@@ -23,6 +23,9 @@ F_RATIO_COH = 1 << 7
 KIND_ADAMW = 0
 KIND_SGD = 1
 
+PEER_SUM_F32 = 0
+PEER_MAX_I32 = 1
+
 ERRORS = {
     -1: "invalid argument",
     -2: "unsupported shape/stride",
@@ -31,6 +34,7 @@ ERRORS = {
     -5: "CUDA launch/runtime error",
     -6: "no usable CUDA device",
     -7: "size above the fixed maximum",
+    -8: "a cross-GPU wait ran out",
 }
 
 
@@ -111,6 +115,18 @@ def make_step_params(kind="adamw", mantissa_bias=15, alpha=0.1, beta1=0.0,
     )
 
 
+class PeerSync(ctypes.Structure):
+    """Mirror of `concord_peer_sync` (include/concord_b200.h)."""
+    _fields_ = [
+        ("flags", ctypes.c_void_p),
+        ("peer_flags", ctypes.c_void_p),
+        ("state", ctypes.c_void_p),
+        ("rank", ctypes.c_int32),
+        ("n_ranks", ctypes.c_int32),
+        ("timeout_ns", ctypes.c_int64),
+    ]
+
+
 _LIB = None
 
 _P = ctypes.c_void_p
@@ -134,6 +150,22 @@ _SIGS = [
     ("concord_step", ctypes.c_int,
      [ctypes.POINTER(StepParams), _P, _I64, _P, _I64, _P, _I64, _P, _P, _P, _P,
       _P, _P, _P, _P, _I64, _P, _P, _P, _I64, _I64, _I64, _P, _P]),
+    ("concord_step_sharded", ctypes.c_int,
+     [ctypes.POINTER(StepParams), _P, _I64, _P, _I64, _P, _I64, _P, _P, _P, _P,
+      _P, _P, _P, _P, _I64, _P, _P, _P, _I64, _I64, _I64, _P, _P, _I32, _P]),
+    ("concord_ipc_handle_bytes", ctypes.c_size_t, []),
+    ("concord_peer_alloc", ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]),
+    ("concord_peer_free", ctypes.c_int, [_P]),
+    ("concord_ipc_export", ctypes.c_int, [_P, _P]),
+    ("concord_ipc_open", ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_void_p)]),
+    ("concord_ipc_close", ctypes.c_int, [_P]),
+    ("concord_peer_push_rows", ctypes.c_int,
+     [_P, _I64, _I64, _I64, _P, ctypes.POINTER(PeerSync), _P]),
+    ("concord_peer_reduce_vhat", ctypes.c_int,
+     [_P, _P, _I64, _I64, _I64, _P, _P, _F, _F, _P, _P, _P, _P, _P, _P, ctypes.c_size_t,
+      ctypes.POINTER(PeerSync), _P]),
+    ("concord_peer_allreduce", ctypes.c_int,
+     [_P, _P, _I64, _I32, _P, _I64, ctypes.POINTER(PeerSync), _P]),
     ("concord_rebalance_workspace_bytes", ctypes.c_size_t, [_I64, _I64]),
     ("concord_rebalance", ctypes.c_int,
      [_P, _I64, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32,

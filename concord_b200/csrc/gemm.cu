@@ -13,7 +13,7 @@
 // TMA producer warp -> shared-memory ring -> one thread issuing
 // tcgen05.mma (cta_group::1, 128x256x64 tiles) into TMEM -> epilogue warps
 // reading TMEM with tcgen05.ld and storing through TMA.  Cluster shape 1x1x1:
-// no TMA multicast is used anywhere (the same kernels run in multi-GPU jobs).
+// every TMA load is a single-CTA load (the same kernels run in multi-GPU jobs).
 #include <cuda_runtime.h>
 
 #include "cute/tensor.hpp"

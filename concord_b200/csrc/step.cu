@@ -342,6 +342,8 @@ struct StepArgs {
     const float* lr; const float* eps; const int32_t* salt;
     int64_t N, K, row0;
     double* coh_stats;
+    const uint64_t* wpeers;  // other ranks' full forward-weight buffers (row stride ldw), or null
+    int32_t npeers;
 };
 
 __device__ __forceinline__ StepScalars load_scalars(const StepArgs& A) {
@@ -405,6 +407,9 @@ __global__ void __launch_bounds__(STEP_THREADS, MINB) step_vec_kernel(StepArgs A
     const bool write_cp = use_cp && (F & CONCORD_F_APPLY_CHASE);
     const bool track = (F & CONCORD_F_TRACK_REBALANCE) != 0;
     const StepScalars S = load_scalars(A);
+    // peer rows start on 16 bytes when the row stride is a multiple of 8 elements
+    // (peer buffers are whole allocations, so their bases are aligned)
+    const bool peer16 = (A.ldw % 8) == 0;
 
     int32_t ce[VEC];
     float vc[VEC];
@@ -446,6 +451,7 @@ __global__ void __launch_bounds__(STEP_THREADS, MINB) step_vec_kernel(StepArgs A
         const int64_t n = rbase + r;
         if (n >= A.N) break;
         int rml = 0;
+        uint2 wb = make_uint2(0u, 0u);
         const int4 w4 = nw4;
         const uint2 g4 = ng4;
         const float4 cpv = ncp;
@@ -511,9 +517,26 @@ __global__ void __launch_bounds__(STEP_THREADS, MINB) step_vec_kernel(StepArgs A
             __stcs(reinterpret_cast<int4*>(pw), make_int4(wv[0], wv[1], wv[2], wv[3]));
             __nv_bfloat162 b01 = __floats2bfloat162_rn(wf[0], wf[1]);
             __nv_bfloat162 b23 = __floats2bfloat162_rn(wf[2], wf[3]);
-            __stcs(reinterpret_cast<uint2*>(A.wbuf + n * A.ldw + k0),
-                   make_uint2(*reinterpret_cast<uint32_t*>(&b01), *reinterpret_cast<uint32_t*>(&b23)));
+            wb = make_uint2(*reinterpret_cast<uint32_t*>(&b01), *reinterpret_cast<uint32_t*>(&b23));
+            __stcs(reinterpret_cast<uint2*>(A.wbuf + n * A.ldw + k0), wb);
             if (write_cp) __stcs(reinterpret_cast<float4*>(pc), make_float4(cp[0], cp[1], cp[2], cp[3]));
+        }
+        if (A.npeers > 0) {
+            // the all-gather of the forward weight: this row's weights into every
+            // other rank's buffer, 16 bytes per even lane (its 4 columns and its
+            // odd neighbour's), 8 bytes where the neighbour has no columns or the
+            // rows are not 16-byte aligned
+            const uint32_t hx = __shfl_down_sync(0xffffffffu, wb.x, 1);
+            const uint32_t hy = __shfl_down_sync(0xffffffffu, wb.y, 1);
+            const bool pair = peer16 && (k0 + VEC) < A.K;
+            if (active && (!peer16 || !(lane & 1))) {
+                const int64_t off = (A.row0 + n) * A.ldw + k0;
+                for (int q = 0; q < A.npeers; ++q) {
+                    uint16_t* dst = reinterpret_cast<uint16_t*>(A.wpeers[q]) + off;
+                    if (pair) __stcs(reinterpret_cast<uint4*>(dst), make_uint4(wb.x, wb.y, hx, hy));
+                    else __stcs(reinterpret_cast<uint2*>(dst), wb);
+                }
+            }
         }
         if (track) {
             int m = warp_max(rml);
@@ -559,7 +582,10 @@ __global__ void __launch_bounds__(STEP_THREADS) step_generic_kernel(StepArgs A) 
                                                 need_vhat ? A.v_row[n] : 0.0f, need_vhat ? A.v_col[k] : 0.0f,
                                                 cp, S, pos);
         A.packed[n * A.ldp + k] = o.word;
-        A.wbuf[n * A.ldw + k] = __bfloat16_as_ushort(__float2bfloat16_rn(o.wval));
+        const uint16_t wb = __bfloat16_as_ushort(__float2bfloat16_rn(o.wval));
+        A.wbuf[n * A.ldw + k] = wb;
+        for (int q = 0; q < A.npeers; ++q)
+            reinterpret_cast<uint16_t*>(A.wpeers[q])[(A.row0 + n) * A.ldw + k] = wb;
         if (write_cp) A.coh_pre[n * A.ldc + k] = o.coh_pre;
         if (track && o.abs_eff > 0) {
             atomicMax(A.row_max + n, o.abs_eff);
@@ -585,15 +611,17 @@ static void launch_vec(bool adamw, uint32_t F, bool has_cp, dim3 grid, cudaStrea
 
 using namespace concord;
 
-extern "C" int concord_step(const concord_step_params* p, int32_t* packed, int64_t ldp,
-                            const uint16_t* grad, int64_t ldg, uint16_t* wbuf, int64_t ldw,
-                            const int8_t* row_exp, const int8_t* col_exp, int32_t* row_max,
-                            int32_t* col_max, const float* v_row, const float* v_col,
-                            const float* sum_v_inv, float* coh_pre, int64_t ldc, const float* lr,
-                            const float* eps, const int32_t* salt, int64_t N, int64_t K,
-                            int64_t row0, double* coh_stats, void* stream) {
+static int step_impl(const concord_step_params* p, int32_t* packed, int64_t ldp,
+                     const uint16_t* grad, int64_t ldg, uint16_t* wbuf, int64_t ldw,
+                     const int8_t* row_exp, const int8_t* col_exp, int32_t* row_max,
+                     int32_t* col_max, const float* v_row, const float* v_col,
+                     const float* sum_v_inv, float* coh_pre, int64_t ldc, const float* lr,
+                     const float* eps, const int32_t* salt, int64_t N, int64_t K,
+                     int64_t row0, double* coh_stats, const uint64_t* wpeers, int32_t npeers,
+                     void* stream) {
     if (!p || !packed || !grad || !wbuf || !row_exp || !col_exp || !lr || !salt)
         return fail(CONCORD_EINVAL, "concord_step: null pointer");
+    if (npeers < 0 || (npeers > 0 && !wpeers)) return fail(CONCORD_EINVAL, "concord_step_sharded: bad peer list");
     if (N < 0 || K < 0 || ldp < K || ldg < K || ldw < K) return fail(CONCORD_ESHAPE, "concord_step: bad shape/stride");
     if (N == 0 || K == 0) return CONCORD_OK;
     if (p->kind != CONCORD_KIND_ADAMW && p->kind != CONCORD_KIND_SGD)
@@ -611,7 +639,8 @@ extern "C" int concord_step(const concord_step_params* p, int32_t* packed, int64
     if (use_cp && ldc < K) return fail(CONCORD_ESHAPE, "concord_step: bad coh_pre stride");
     if (row0 < 0 || row0 + N > (int64_t)1 << 31) return fail(CONCORD_ESHAPE, "concord_step: row index beyond int32");
     StepArgs A{*p, packed, ldp, grad, ldg, wbuf, ldw, row_exp, col_exp, row_max, col_max,
-               v_row, v_col, sum_v_inv, coh_pre, ldc, lr, eps, salt, N, K, row0, coh_stats};
+               v_row, v_col, sum_v_inv, coh_pre, ldc, lr, eps, salt, N, K, row0, coh_stats,
+               wpeers, npeers};
     bool vec = (K % VEC == 0) && (ldp % VEC == 0) && (ldg % VEC == 0) && (ldw % VEC == 0) &&
                aligned(packed, 16) && aligned(grad, 8) && aligned(wbuf, 8) && aligned(col_exp, 4);
     if (need_vhat) vec = vec && aligned(v_col, 16);
@@ -634,4 +663,28 @@ extern "C" int concord_step(const concord_step_params* p, int32_t* packed, int64
         else step_generic_kernel<CONCORD_KIND_SGD><<<(unsigned)blocks, STEP_THREADS, 0, s>>>(A);
     }
     return check_launch("concord_step");
+}
+
+extern "C" int concord_step(const concord_step_params* p, int32_t* packed, int64_t ldp,
+                            const uint16_t* grad, int64_t ldg, uint16_t* wbuf, int64_t ldw,
+                            const int8_t* row_exp, const int8_t* col_exp, int32_t* row_max,
+                            int32_t* col_max, const float* v_row, const float* v_col,
+                            const float* sum_v_inv, float* coh_pre, int64_t ldc, const float* lr,
+                            const float* eps, const int32_t* salt, int64_t N, int64_t K,
+                            int64_t row0, double* coh_stats, void* stream) {
+    return step_impl(p, packed, ldp, grad, ldg, wbuf, ldw, row_exp, col_exp, row_max, col_max, v_row, v_col,
+                     sum_v_inv, coh_pre, ldc, lr, eps, salt, N, K, row0, coh_stats, nullptr, 0, stream);
+}
+
+extern "C" int concord_step_sharded(const concord_step_params* p, int32_t* packed, int64_t ldp,
+                                    const uint16_t* grad, int64_t ldg, uint16_t* wbuf, int64_t ldw,
+                                    const int8_t* row_exp, const int8_t* col_exp, int32_t* row_max,
+                                    int32_t* col_max, const float* v_row, const float* v_col,
+                                    const float* sum_v_inv, float* coh_pre, int64_t ldc, const float* lr,
+                                    const float* eps, const int32_t* salt, int64_t N, int64_t K,
+                                    int64_t row0, double* coh_stats, const uint64_t* wbuf_peers,
+                                    int32_t n_peers, void* stream) {
+    return step_impl(p, packed, ldp, grad, ldg, wbuf, ldw, row_exp, col_exp, row_max, col_max, v_row, v_col,
+                     sum_v_inv, coh_pre, ldc, lr, eps, salt, N, K, row0, coh_stats, wbuf_peers, n_peers,
+                     stream);
 }

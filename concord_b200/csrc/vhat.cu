@@ -18,6 +18,7 @@
 // reference does with separate launches before its apply kernel
 // (packed_b.py:1281-1283, 910-911).
 #include "common.cuh"
+#include "peer.cuh"
 
 namespace concord {
 
@@ -38,8 +39,23 @@ struct VhatArgs {
     bool vec;
     float* col_sum_out;  // shard mode: raw column sums of g^2 (v_col untouched)
     float* vsum_out;     // shard mode: sum of this shard's updated v_row
+    // peer mode (template P >= 1): the gradient rows are the fp32 rank-order
+    // sum of P ranks' bf16 rows, rounded to bf16 and written to grad (row
+    // stride ldg) as they are read.  Rank q's rows: `own` (this rank's dW rows
+    // of its shard) for q == rank, else block q of the receive buffer
+    // (recv + q*S*K); row stride K
+    const uint16_t* own;
+    const uint16_t* recv;
+    int64_t S;
+    PeerSync sync;
 };
 
+// rows of one load group: all 16 rows of a warp at once for a local gradient,
+// fewer when each row is P loads from peers
+template <int P>
+struct VhGroup { static constexpr int G = P <= 1 ? 16 : (P <= 2 ? 8 : (P <= 4 ? 4 : 2)); };
+
+template <int P>
 __global__ void __launch_bounds__(VH_THREADS) vhat_kernel(VhatArgs A) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int cs = blockIdx.x, rb = blockIdx.y;
@@ -48,6 +64,8 @@ __global__ void __launch_bounds__(VH_THREADS) vhat_kernel(VhatArgs A) {
     __shared__ float red[VH_THREADS];
     __shared__ int flags[2];
 
+    // every rank's push of this epoch has landed in the receive buffer
+    if (P > 0 && !peer_wait(A.sync, ld_volatile(A.sync.state))) return;  // leave everything untouched
     if (A.salt && cs == 0 && rb == 0 && threadIdx.x == 0) *A.salt += 1;
     if (A.row_max && cs == 0 && threadIdx.x < VH_ROWS) {
         int64_t n = (int64_t)rb * VH_ROWS + threadIdx.x;
@@ -61,51 +79,86 @@ __global__ void __launch_bounds__(VH_THREADS) vhat_kernel(VhatArgs A) {
     float cacc[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) cacc[j] = 0.0f;
-    // issue all of this warp's row loads before any arithmetic (vector path)
-    uint4 raw[VH_ROWS / 8];
-    if (A.vec && k0 < A.K) {
+    constexpr int G = VhGroup<P>::G;
+    const bool vec_ok = A.vec && k0 < A.K;
 #pragma unroll
-        for (int i = 0; i < VH_ROWS / 8; ++i) {
-            const int64_t n = (int64_t)rb * VH_ROWS + warp + 8 * i;
-            raw[i] = n < A.N ? __ldcs(reinterpret_cast<const uint4*>(A.grad + n * A.ldg + k0))
-                             : make_uint4(0, 0, 0, 0);
-        }
-    }
+    for (int i0 = 0; i0 < VH_ROWS / 8; i0 += G) {
+        // issue the group's loads before any arithmetic (vector path)
+        uint4 raw[G];
+        if (P == 0) {
+            if (vec_ok) {
 #pragma unroll
-    for (int i = 0; i < VH_ROWS / 8; ++i) {
-        const int64_t n = (int64_t)rb * VH_ROWS + warp + 8 * i;
-        float g2[8];
-        if (n < A.N) {
-            const uint16_t* gp = A.grad + n * A.ldg + k0;
-            if (A.vec && k0 < A.K) {
-                const uint4 v = raw[i];
-                uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    float g = bf16_to_f32((w[j >> 1] >> ((j & 1) * 16)) & 0xffffu);
-                    g2[j] = g * g;
-                }
-            } else {
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    float g = (k0 + j < A.K) ? bf16_to_f32(gp[j]) : 0.0f;
-                    g2[j] = g * g;
+                for (int u = 0; u < G; ++u) {
+                    const int64_t n = (int64_t)rb * VH_ROWS + warp + 8 * (i0 + u);
+                    raw[u] = n < A.N ? __ldcs(reinterpret_cast<const uint4*>(A.grad + n * A.ldg + k0))
+                                     : make_uint4(0, 0, 0, 0);
                 }
             }
         } else {
+            constexpr int PP = P > 0 ? P : 1;
+            uint4 pv[G][PP];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) g2[j] = 0.0f;
+            for (int u = 0; u < G; ++u) {
+                const int64_t n = (int64_t)rb * VH_ROWS + warp + 8 * (i0 + u);
+                if (n < A.N && k0 < A.K) {
+#pragma unroll
+                    for (int q = 0; q < PP; ++q) {
+                        const uint16_t* src = q == A.sync.rank ? A.own : A.recv + (int64_t)q * A.S * A.K;
+                        pv[u][q] = __ldcs(reinterpret_cast<const uint4*>(src + n * A.K + k0));
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < G; ++u) {
+                const int64_t n = (int64_t)rb * VH_ROWS + warp + 8 * (i0 + u);
+                raw[u] = make_uint4(0, 0, 0, 0);
+                if (n < A.N && k0 < A.K) {
+                    float acc[8];
+                    set_bf16x8(acc, pv[u][0]);
+#pragma unroll
+                    for (int q = 1; q < PP; ++q) add_bf16x8(acc, pv[u][q]);
+                    raw[u] = pack_bf16x8(acc);
+                    __stcs(reinterpret_cast<uint4*>(const_cast<uint16_t*>(A.grad) + n * A.ldg + k0), raw[u]);
+                }
+            }
         }
-        // row partial: lane sum of 8 columns, then xor butterfly
-        float s = g2[0];
 #pragma unroll
-        for (int j = 1; j < 8; ++j) s = s + g2[j];
+        for (int u = 0; u < G; ++u) {
+            const int i = i0 + u;
+            const int64_t n = (int64_t)rb * VH_ROWS + warp + 8 * i;
+            float g2[8];
+            if (n < A.N) {
+                const uint16_t* gp = A.grad + n * A.ldg + k0;
+                if (P > 0 || vec_ok) {
+                    const uint4 v = raw[u];
+                    uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) s = s + __shfl_xor_sync(0xffffffffu, s, o);
-        if (lane == 0 && n < A.N) A.rp[(int64_t)cs * A.N + n] = s;
-        // column partial: this warp's rows in order
+                    for (int j = 0; j < 8; ++j) {
+                        float g = bf16_to_f32((w[j >> 1] >> ((j & 1) * 16)) & 0xffffu);
+                        g2[j] = g * g;
+                    }
+                } else {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) cacc[j] = (i == 0) ? g2[j] : cacc[j] + g2[j];
+                    for (int j = 0; j < 8; ++j) {
+                        float g = (k0 + j < A.K) ? bf16_to_f32(gp[j]) : 0.0f;
+                        g2[j] = g * g;
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) g2[j] = 0.0f;
+            }
+            // row partial: lane sum of 8 columns, then xor butterfly
+            float s = g2[0];
+#pragma unroll
+            for (int j = 1; j < 8; ++j) s = s + g2[j];
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) s = s + __shfl_xor_sync(0xffffffffu, s, o);
+            if (lane == 0 && n < A.N) A.rp[(int64_t)cs * A.N + n] = s;
+            // column partial: this warp's rows in order
+#pragma unroll
+            for (int j = 0; j < 8; ++j) cacc[j] = (i == 0) ? g2[j] : cacc[j] + g2[j];
+        }
     }
 #pragma unroll
     for (int j = 0; j < 8; ++j) colsm[warp][lane * 8 + j] = cacc[j];
@@ -131,8 +184,17 @@ __global__ void __launch_bounds__(VH_THREADS) vhat_kernel(VhatArgs A) {
         __threadfence();
         const int64_t col = (int64_t)cs * VH_COLS + threadIdx.x;
         if (col < A.K) {
+            // fixed order b = 0, 1, ..., nrb-1; the loads of 8 partials go out together
             float t = __ldcg(A.cp + col);
-            for (int b = 1; b < A.nrb; ++b) t = t + __ldcg(A.cp + (int64_t)b * A.K + col);
+            int b = 1;
+            for (; b + 8 <= A.nrb; b += 8) {
+                float v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) v[u] = __ldcg(A.cp + (int64_t)(b + u) * A.K + col);
+#pragma unroll
+                for (int u = 0; u < 8; ++u) t = t + v[u];
+            }
+            for (; b < A.nrb; ++b) t = t + __ldcg(A.cp + (int64_t)b * A.K + col);
             if (A.col_sum_out) A.col_sum_out[col] = t;
             else A.v_col[col] = A.b2 * A.v_col[col] + A.omb2 * t;
         }
@@ -157,8 +219,17 @@ __global__ void __launch_bounds__(VH_THREADS) vhat_kernel(VhatArgs A) {
         __syncthreads();
         if (flags[0]) {
             __threadfence();
+            // fixed order n = t, t+256, t+512, ...; the loads of 8 go out together
             float acc = 0.0f;
-            for (int64_t n = threadIdx.x; n < A.N; n += VH_THREADS) acc = acc + __ldcg(A.v_row + n);
+            int64_t n = threadIdx.x;
+            for (; n + 7 * VH_THREADS < A.N; n += 8 * VH_THREADS) {
+                float v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) v[u] = __ldcg(A.v_row + n + u * VH_THREADS);
+#pragma unroll
+                for (int u = 0; u < 8; ++u) acc = acc + v[u];
+            }
+            for (; n < A.N; n += VH_THREADS) acc = acc + __ldcg(A.v_row + n);
             red[threadIdx.x] = acc;
             __syncthreads();
             for (int s = VH_THREADS / 2; s >= 1; s >>= 1) {
@@ -222,9 +293,10 @@ static int vhat_launch(const uint16_t* grad, int64_t ldg, int64_t N, int64_t K, 
     VhatArgs A{grad, ldg, N, K, v_row, v_col, sum_v_inv, beta2, one_minus_beta2, row_max, col_max, salt,
                reinterpret_cast<float*>(ws + off_rp), reinterpret_cast<float*>(ws + off_cp),
                reinterpret_cast<unsigned*>(ws), ncs, nrb,
-               (K % 8 == 0) && (ldg % 8 == 0) && aligned(grad, 16), col_sum_out, vsum_out};
+               (K % 8 == 0) && (ldg % 8 == 0) && aligned(grad, 16), col_sum_out, vsum_out,
+               nullptr, nullptr, 0, PeerSync{}};
     dim3 grid((unsigned)ncs, (unsigned)nrb);
-    vhat_kernel<<<grid, VH_THREADS, 0, as_stream(stream)>>>(A);
+    vhat_kernel<0><<<grid, VH_THREADS, 0, as_stream(stream)>>>(A);
     return check_launch(name);
 }
 
@@ -245,6 +317,54 @@ extern "C" int concord_vhat_partial(const uint16_t* grad, int64_t ldg, int64_t N
     if (!grad || !v_row || !col_sum_out || !vsum_out) return fail(CONCORD_EINVAL, "concord_vhat_partial: null pointer");
     return vhat_launch(grad, ldg, N, K, v_row, nullptr, nullptr, beta2, one_minus_beta2, row_max, col_max, salt,
                        col_sum_out, vsum_out, workspace, workspace_bytes, stream, "concord_vhat_partial");
+}
+
+template <int P>
+static void launch_peer_vhat(dim3 grid, cudaStream_t st, const VhatArgs& A) {
+    vhat_kernel<P><<<grid, VH_THREADS, 0, st>>>(A);
+}
+
+extern "C" int concord_peer_reduce_vhat(const uint16_t* own_rows, const uint16_t* recv, int64_t S, int64_t K,
+                                        int64_t n_rows, uint16_t* grad_out, float* v_row, float beta2,
+                                        float one_minus_beta2, int32_t* row_max, int32_t* col_max, int32_t* salt,
+                                        float* col_sum_out, float* vsum_out, void* workspace,
+                                        size_t workspace_bytes, const concord_peer_sync* sync, void* stream) {
+    const char* name = "concord_peer_reduce_vhat";
+    if ((n_rows > 0 && (!own_rows || !recv)) || !grad_out || !v_row || !col_sum_out || !vsum_out || !sync || !sync->flags ||
+        !sync->peer_flags || !sync->state)
+        return fail(CONCORD_EINVAL, std::string(name) + ": null pointer");
+    if (sync->n_ranks < 1 || sync->n_ranks > PEER_MAX_RANKS || sync->rank < 0 || sync->rank >= sync->n_ranks)
+        return fail(CONCORD_EINVAL, std::string(name) + ": n_ranks must be 1..8 and rank < n_ranks");
+    if (sync->timeout_ns <= 0) return fail(CONCORD_EINVAL, std::string(name) + ": timeout_ns must be > 0");
+    if (K <= 0 || K % 8 != 0 || n_rows < 0 || n_rows > S)
+        return fail(CONCORD_ESHAPE, std::string(name) + ": K must be a positive multiple of 8 and n_rows <= S");
+    if (!aligned(grad_out, 16) || (n_rows > 0 && (!aligned(own_rows, 16) || !aligned(recv, 16))))
+        return fail(CONCORD_EALIGN, std::string(name) + ": buffers must be 16-byte aligned");
+    // a rank with no rows still takes part: one row block of masked rows gives zero partials
+    int ncs, nrb; size_t off_rp, off_cp, total;
+    vhat_layout(n_rows > 0 ? n_rows : 1, K, &ncs, &nrb, &off_rp, &off_cp, &total);
+    if (!workspace || workspace_bytes < total)
+        return fail(CONCORD_EWORKSPACE, std::string(name) + ": workspace smaller than "
+                                        "concord_vhat_workspace_bytes(max(n_rows, 1), K)");
+    if (nrb > 65535) return fail(CONCORD_ETOOBIG, std::string(name) + ": too many rows for one launch");
+    char* ws = static_cast<char*>(workspace);
+    VhatArgs A{grad_out, K, n_rows, K, v_row, nullptr, nullptr, beta2, one_minus_beta2, row_max, col_max, salt,
+               reinterpret_cast<float*>(ws + off_rp), reinterpret_cast<float*>(ws + off_cp),
+               reinterpret_cast<unsigned*>(ws), ncs, nrb, true, col_sum_out, vsum_out, own_rows, recv, S,
+               PeerSync{sync->flags, sync->peer_flags, sync->state, sync->rank, sync->n_ranks, sync->timeout_ns}};
+    dim3 grid((unsigned)ncs, (unsigned)nrb);
+    cudaStream_t st = as_stream(stream);
+    switch (sync->n_ranks) {
+        case 1: launch_peer_vhat<1>(grid, st, A); break;
+        case 2: launch_peer_vhat<2>(grid, st, A); break;
+        case 3: launch_peer_vhat<3>(grid, st, A); break;
+        case 4: launch_peer_vhat<4>(grid, st, A); break;
+        case 5: launch_peer_vhat<5>(grid, st, A); break;
+        case 6: launch_peer_vhat<6>(grid, st, A); break;
+        case 7: launch_peer_vhat<7>(grid, st, A); break;
+        default: launch_peer_vhat<8>(grid, st, A); break;
+    }
+    return check_launch(name);
 }
 
 extern "C" int concord_vhat_finish(const float* col_sum, const float* vsum, float* v_col, float* sum_v_inv,

@@ -197,18 +197,26 @@ def materialize_packed_bf16(packed_w, row_exp, col_exp, out, mantissa_bias=15,
 
 
 def _step_launch(params, packed_w, grad_W, weight_buf, row_exp, col_exp, row_max, col_max,
-                 v_row, v_col, sum_v_inv, coh_pre, lr_t, eps_t, salt, row0=0, coh_stats=None):
+                 v_row, v_col, sum_v_inv, coh_pre, lr_t, eps_t, salt, row0=0, coh_stats=None,
+                 wbuf_peers=None):
+    """One concord_step launch; with `wbuf_peers` (int64 device tensor of other
+    ranks' forward-weight base addresses) the step also stores every bf16
+    weight it writes into those buffers (concord_step_sharded)."""
     N, K = packed_w.shape
     assert packed_w.stride(1) == 1 and grad_W.stride(1) == 1 and weight_buf.stride(1) == 1
     _need_cuda(packed_w, grad_W, weight_buf, row_exp, col_exp, row_max, col_max, v_row, v_col,
                sum_v_inv, coh_pre, lr_t, eps_t, salt)
     lib = _lib()
-    _abi.check(lib.concord_step(
-        ctypes.byref(params), _ptr(packed_w), packed_w.stride(0), _ptr(grad_W), grad_W.stride(0),
-        _ptr(weight_buf), weight_buf.stride(0), _ptr(row_exp), _ptr(col_exp), _ptr(row_max),
-        _ptr(col_max), _ptr(v_row), _ptr(v_col), _ptr(sum_v_inv), _ptr(coh_pre),
-        coh_pre.stride(0) if coh_pre is not None else K, _ptr(lr_t), _ptr(eps_t), _ptr(salt),
-        N, K, int(row0), _ptr(coh_stats), _stream(packed_w.device)), "concord_step")
+    args = (ctypes.byref(params), _ptr(packed_w), packed_w.stride(0), _ptr(grad_W), grad_W.stride(0),
+            _ptr(weight_buf), weight_buf.stride(0), _ptr(row_exp), _ptr(col_exp), _ptr(row_max),
+            _ptr(col_max), _ptr(v_row), _ptr(v_col), _ptr(sum_v_inv), _ptr(coh_pre),
+            coh_pre.stride(0) if coh_pre is not None else K, _ptr(lr_t), _ptr(eps_t), _ptr(salt),
+            N, K, int(row0), _ptr(coh_stats))
+    if wbuf_peers is not None and wbuf_peers.numel() > 0:
+        _abi.check(lib.concord_step_sharded(*args, _ptr(wbuf_peers), int(wbuf_peers.numel()),
+                                            _stream(packed_w.device)), "concord_step_sharded")
+    else:
+        _abi.check(lib.concord_step(*args, _stream(packed_w.device)), "concord_step")
 
 
 def _salt_bump(salt):

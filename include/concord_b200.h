@@ -39,6 +39,8 @@
  *                            (packed_b.py:2081-2106)
  *   concord_gemm_fwd/dx/dw <- F.linear / grad_y @ W / grad_y^T @ x
  *                            (packed_b.py:1219, 1263, 1271-1277)
+ * The peer-memory entry points (concord_peer_*, concord_ipc_*,
+ * concord_step_sharded) have no counterpart: the reference is single-GPU.
  */
 #ifndef CONCORD_B200_H
 #define CONCORD_B200_H
@@ -61,6 +63,7 @@ extern "C" {
 #define CONCORD_ELAUNCH      -5  /* CUDA launch / runtime error               */
 #define CONCORD_ENODEVICE    -6  /* no usable CUDA device                      */
 #define CONCORD_ETOOBIG      -7  /* size above a fixed maximum                */
+#define CONCORD_ETIMEOUT     -8  /* a cross-GPU wait ran out (peer transport)  */
 
 /* step-kernel flag bits (the reference's Triton constexprs, packed_b.py:451-458) */
 #define CONCORD_F_MASS_PRESERVE   (1u << 0)
@@ -192,6 +195,110 @@ int concord_step(const concord_step_params* p,
                  const float* lr, const float* eps, const int32_t* salt,
                  int64_t N, int64_t K, int64_t row0,
                  double* coh_stats, void* stream);
+
+/*
+ * concord_step for a row shard in a data-parallel job whose ranks share
+ * memory over NVLink (no reference counterpart).  Identical to concord_step,
+ * and in addition every bf16 weight the step writes to wbuf (rows [0,N) of
+ * the shard) is also stored to row row0 + n of each of the n_peers other
+ * ranks' full forward-weight buffers: wbuf_peers is a DEVICE array of their
+ * base addresses (opened with concord_ipc_open), each with row stride ldw.
+ * This is the all-gather of the forward weight, overlapped with the step.
+ */
+int concord_step_sharded(const concord_step_params* p,
+                         int32_t* packed, int64_t ldp,
+                         const uint16_t* grad, int64_t ldg,
+                         uint16_t* wbuf, int64_t ldw,
+                         const int8_t* row_exp, const int8_t* col_exp,
+                         int32_t* row_max, int32_t* col_max,
+                         const float* v_row, const float* v_col, const float* sum_v_inv,
+                         float* coh_pre, int64_t ldc,
+                         const float* lr, const float* eps, const int32_t* salt,
+                         int64_t N, int64_t K, int64_t row0,
+                         double* coh_stats, const uint64_t* wbuf_peers, int32_t n_peers,
+                         void* stream);
+
+/*
+ * Peer memory for the data-parallel step over NVLink (no reference
+ * counterpart).  concord_peer_alloc / concord_peer_free: plain device
+ * allocations of the current device (zero-filled), exportable whole with
+ * concord_ipc_export into a concord_ipc_handle_bytes()-byte handle that
+ * another process on the same node maps with concord_ipc_open (and unmaps
+ * with concord_ipc_close).
+ */
+size_t concord_ipc_handle_bytes(void);
+int concord_peer_alloc(size_t bytes, void** dev_ptr);
+int concord_peer_free(void* dev_ptr);
+int concord_ipc_export(void* dev_ptr, void* handle_out);
+int concord_ipc_open(const void* handle, void** dev_ptr);
+int concord_ipc_close(void* dev_ptr);
+
+/*
+ * Cross-GPU rendezvous state of one peer-memory exchange (device memory):
+ *   flags      this rank's flag array [n_ranks] in peer memory; rank q
+ *              stores its epoch into flags[q]
+ *   peer_flags DEVICE array [n_ranks] of every rank's flag array (own included)
+ *   state      this rank's int32[4]: [0] epoch, [1] finished-block count,
+ *              [2] error word (non-zero after a wait ran out; sticky until
+ *              the caller clears it), [3] unused; zero-filled at creation
+ * Every wait polls with a limit of timeout_ns of GPU time; when it runs out
+ * the kernel sets state[2], skips its work and returns, so the context
+ * stays usable and the host sees the error word.
+ */
+typedef struct concord_peer_sync {
+    int32_t* flags;
+    const uint64_t* peer_flags;
+    int32_t* state;
+    int32_t rank;
+    int32_t n_ranks;
+    int64_t timeout_ns;
+} concord_peer_sync;
+
+/*
+ * Reduce-scatter of the bf16 dW over peer memory, in two launches.  Ranks own
+ * row shards [q*S, min(N, (q+1)*S)) of an [N, K] gradient (S * n_ranks >= N).
+ *
+ * concord_peer_push_rows: for every q != rank, the rows of q's shard of this
+ * rank's dW (grad, [N, K], row stride K) are stored into q's receive buffer at
+ * block `rank` (recv_q + rank * S * K, row stride K); recv is a DEVICE array
+ * [n_ranks] of every rank's receive buffer (n_ranks * S * K bf16 each).  It
+ * never waits: when all its stores have landed it announces a new epoch to
+ * every rank.
+ *
+ * concord_peer_reduce_vhat: waits until every rank has announced that epoch
+ * (its pushes into this rank's receive buffer have landed), then
+ *   grad_out[n, k] = bf16_rne( sum over q = 0..n_ranks-1, in rank order, in
+ *                    fp32, of src_q[n * K + k] ),   n < n_rows, k < K,
+ * src_rank = own_rows (this rank's rows of its own shard), src_q = recv + q*S*K
+ * (the local receive buffer) otherwise, and in the same pass the v-hat
+ * partials of concord_vhat_partial on grad_out, in the same fixed order: every
+ * output (grad_out, v_row, row_max/col_max zeroing, salt bump, col_sum_out,
+ * vsum_out) is bit-identical to the two steps run separately.  n_rows may be
+ * 0 (a rank without rows: zero partials).  workspace: at least
+ * concord_vhat_workspace_bytes(max(n_rows, 1), K) bytes, zero-filled before
+ * first use.  After a wait ran out nothing is written.  K a multiple of 8;
+ * every buffer 16-byte aligned; n_ranks <= 8.
+ */
+int concord_peer_push_rows(const uint16_t* grad, int64_t N, int64_t K, int64_t S, const uint64_t* recv,
+                           const concord_peer_sync* sync, void* stream);
+int concord_peer_reduce_vhat(const uint16_t* own_rows, const uint16_t* recv, int64_t S, int64_t K,
+                             int64_t n_rows, uint16_t* grad_out, float* v_row, float beta2,
+                             float one_minus_beta2, int32_t* row_max, int32_t* col_max, int32_t* salt,
+                             float* col_sum_out, float* vsum_out, void* workspace, size_t workspace_bytes,
+                             const concord_peer_sync* sync, void* stream);
+
+/*
+ * All-reduce of `count` 32-bit values over the ranks of `sync` through peer
+ * slots (count 0: a pure rendezvous).  op CONCORD_PEER_SUM_F32: fp32 sum in
+ * rank order (the same bits on every rank for any rank count);
+ * CONCORD_PEER_MAX_I32: int32 max.  slots: DEVICE array [n_ranks] of every
+ * rank's slot buffer of 2 * n_ranks * slot_count 32-bit values (concord_peer_alloc,
+ * opened with concord_ipc_open); count <= slot_count.  out may alias in.
+ */
+#define CONCORD_PEER_SUM_F32 0
+#define CONCORD_PEER_MAX_I32 1
+int concord_peer_allreduce(const void* in, void* out, int64_t count, int32_t op, const uint64_t* slots,
+                           int64_t slot_count, const concord_peer_sync* sync, void* stream);
 
 /*
  * Rebalance ratchet.  Folds row_max/col_max into the high-watermarks (when

@@ -1,9 +1,13 @@
-"""Row-sharded data-parallel step on 2 GPUs over NCCL (skipped with fewer GPUs).
+"""Row-sharded data-parallel step on 2 (and 4) GPUs (skipped with fewer GPUs).
 
-Both ranks must end with identical packed words, exponents, v-hat state and
+Every rank must end with identical packed words, exponents, v-hat state and
 forward weight, equal bit for bit to a one-GPU emulation of the same sharded
-arithmetic through the same CUDA kernels.  NVLS is switched off
-(NCCL_NVLS_ENABLE=0) as the pool's rules ask for multi-rank tests.
+arithmetic through the same CUDA kernels (the reduced gradient of the
+emulation is the fp32 sum of the ranks' partials in rank order, rounded once
+to bf16).  Both transports: "collective" (NCCL reduce-scatter / all-gather;
+at 2 ranks NCCL's bf16 sum rounds once, like the emulation) and "peer"
+(NVLink loads and stores through CUDA IPC mappings).  NVLS is switched off
+(NCCL_NVLS_ENABLE=0) in every multi-rank test.
 """
 import os
 import socket
@@ -41,7 +45,7 @@ def _state(layer):
     return out
 
 
-def _worker(rank, world, port, out_dir, N):
+def _worker(rank, world, port, out_dir, N, transport):
     import sys
     sys.path.insert(0, ROOT)
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -50,13 +54,16 @@ def _worker(rank, world, port, out_dir, N):
     from concord_b200.distributed import RowShardedStep
     dev = torch.device("cuda", rank)
     layer = _layer(N, dev)
-    st = RowShardedStep(layer)
+    st = RowShardedStep(layer, transport=transport)
+    assert st.transport == transport
     for s in range(STEPS):
         st.step(_grad(N, s, rank, dev))
         st.rebalance()
+    st.check()
     st.gather_state()
     torch.cuda.synchronize()
     np.savez(os.path.join(out_dir, f"rank{rank}.npz"), **_state(layer))
+    st.close()
     dist.barrier()
     dist.destroy_process_group()
 
@@ -110,14 +117,16 @@ def _free_port():
     return p
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("world,transport", [(2, "collective"), (2, "peer"), (4, "peer")])
 @pytest.mark.parametrize("N", [300, 301])   # even split (in-place collectives) and padded
-def test_row_sharded_step_two_gpus(tmp_path, N):
-    world = 2
-    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path), N), nprocs=world,
-                       join=True, start_method="spawn")
+def test_row_sharded_step(tmp_path, N, world, transport):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path), N, transport),
+                       nprocs=world, join=True, start_method="spawn")
     r = [dict(np.load(tmp_path / f"rank{i}.npz")) for i in range(world)]
     ref = _emulate(world, N)
     for key in ref:
-        np.testing.assert_array_equal(r[0][key], r[1][key], err_msg=key)
+        for i in range(1, world):
+            np.testing.assert_array_equal(r[0][key], r[i][key], err_msg=key)
         np.testing.assert_array_equal(r[0][key], ref[key], err_msg=key)
