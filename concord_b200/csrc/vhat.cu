@@ -4,17 +4,17 @@
 // (concord/packed_b.py:1288-1303):
 //   v_row = b2*v_row + (1-b2)*sum_k g^2;  v_col = b2*v_col + (1-b2)*sum_n g^2;
 //   sum_v_inv = 1 / max(sum_n v_row, 1e-30)
-// in one launch that reads the bf16 gradient once.  Grid: (column slabs of
-// 256, row blocks of 128); each block writes a row partial per (row, slab)
-// and a column partial per (column, row block) into the workspace.  The last
-// block to finish a slab folds that slab's column partials into v_col; the
-// last block to finish a row block folds its row partials into v_row; the
-// last row block overall computes sum_v_inv.  "Last" is decided by atomic
-// arrival counters, so nothing spins.  Every sum runs in a fixed order
+// in two launches that read the bf16 gradient once.  The first: tiles of
+// (column slabs of 256) x (row blocks of 128), taken by a persistent grid of
+// blocks; each tile writes a row partial per (row, slab) and a column partial
+// per (column, row block) into the workspace.  The second folds them: v_col
+// from the column partials in row-block order, v_row from the row partials
+// in slab order, and, in the block that finishes last (an atomic arrival
+// counter, so nothing spins), sum_v_inv.  Every sum runs in a fixed order
 // (spelled out in oracle/concord_oracle.c:oracle_vhat), so the result is
 // deterministic and bit-identical to the CPU restatement.
 //
-// The launch also zeroes row_max/col_max and bumps the step salt, which the
+// The first launch also zeroes row_max/col_max and bumps the step salt, which the
 // reference does with separate launches before its apply kernel
 // (packed_b.py:1281-1283, 910-911).
 #include "common.cuh"
@@ -50,22 +50,28 @@ struct VhatArgs {
     PeerSync sync;
 };
 
-// rows of one load group: all 16 rows of a warp at once for a local gradient,
-// fewer when each row is P loads from peers
+// rows of a warp whose loads go out together: 8 for a local gradient, fewer
+// when each row is the sum of P ranks' rows
 template <int P>
-struct VhGroup { static constexpr int G = P <= 1 ? 16 : (P <= 2 ? 8 : (P <= 4 ? 4 : 2)); };
+struct VhGroup { static constexpr int G = P == 0 ? 8 : (P <= 4 ? 2 : 1); };
 
+constexpr int VH_BLOCKS_PER_SM = 3;
+
+// Persistent: block b takes tiles b, b + gridDim.x, ...; tile t covers
+// column slab t % ncs and row block t / ncs.  Which block computes a tile
+// changes nothing in the arithmetic: every partial and every final sum has
+// a fixed order.
 template <int P>
-__global__ void __launch_bounds__(VH_THREADS) vhat_kernel(VhatArgs A) {
+__global__ void __launch_bounds__(VH_THREADS, VH_BLOCKS_PER_SM) vhat_kernel(VhatArgs A) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int cs = blockIdx.x, rb = blockIdx.y;
-    const int64_t k0 = (int64_t)cs * VH_COLS + lane * 8;
     __shared__ float colsm[VH_THREADS / 32][VH_COLS];
-    __shared__ float red[VH_THREADS];
-    __shared__ int flags[2];
 
     // every rank's push of this epoch has landed in the receive buffer
     if (P > 0 && !peer_wait(A.sync, ld_volatile(A.sync.state))) return;  // leave everything untouched
+    const int ntiles = A.ncs * A.nrb;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    const int cs = tile % A.ncs, rb = tile / A.ncs;
+    const int64_t k0 = (int64_t)cs * VH_COLS + lane * 8;
     if (A.salt && cs == 0 && rb == 0 && threadIdx.x == 0) *A.salt += 1;
     if (A.row_max && cs == 0 && threadIdx.x < VH_ROWS) {
         int64_t n = (int64_t)rb * VH_ROWS + threadIdx.x;
@@ -95,16 +101,35 @@ __global__ void __launch_bounds__(VH_THREADS) vhat_kernel(VhatArgs A) {
                 }
             }
         } else {
+            // sources in chunks of at most 4 (loads of a chunk go out together),
+            // added in rank order into fp32 accumulators
             constexpr int PP = P > 0 ? P : 1;
-            uint4 pv[G][PP];
+            constexpr int QC = PP < 4 ? PP : 4;
+            float acc[G][8];
 #pragma unroll
-            for (int u = 0; u < G; ++u) {
-                const int64_t n = (int64_t)rb * VH_ROWS + warp + 8 * (i0 + u);
-                if (n < A.N && k0 < A.K) {
+            for (int q0 = 0; q0 < PP; q0 += QC) {
+                uint4 pv[G][QC];
 #pragma unroll
-                    for (int q = 0; q < PP; ++q) {
-                        const uint16_t* src = q == A.sync.rank ? A.own : A.recv + (int64_t)q * A.S * A.K;
-                        pv[u][q] = __ldcs(reinterpret_cast<const uint4*>(src + n * A.K + k0));
+                for (int u = 0; u < G; ++u) {
+                    const int64_t n = (int64_t)rb * VH_ROWS + warp + 8 * (i0 + u);
+                    if (n < A.N && k0 < A.K) {
+#pragma unroll
+                        for (int c = 0; c < QC; ++c) {
+                            const int q = q0 + c;
+                            if (q < PP) {
+                                const uint16_t* src = q == A.sync.rank ? A.own : A.recv + (int64_t)q * A.S * A.K;
+                                pv[u][c] = __ldcs(reinterpret_cast<const uint4*>(src + n * A.K + k0));
+                            }
+                        }
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < G; ++u) {
+#pragma unroll
+                    for (int c = 0; c < QC; ++c) {
+                        const int q = q0 + c;
+                        if (q == 0) set_bf16x8(acc[u], pv[u][c]);
+                        else if (q < PP) add_bf16x8(acc[u], pv[u][c]);
                     }
                 }
             }
@@ -113,15 +138,12 @@ __global__ void __launch_bounds__(VH_THREADS) vhat_kernel(VhatArgs A) {
                 const int64_t n = (int64_t)rb * VH_ROWS + warp + 8 * (i0 + u);
                 raw[u] = make_uint4(0, 0, 0, 0);
                 if (n < A.N && k0 < A.K) {
-                    float acc[8];
-                    set_bf16x8(acc, pv[u][0]);
-#pragma unroll
-                    for (int q = 1; q < PP; ++q) add_bf16x8(acc, pv[u][q]);
-                    raw[u] = pack_bf16x8(acc);
+                    raw[u] = pack_bf16x8(acc[u]);
                     __stcs(reinterpret_cast<uint4*>(const_cast<uint16_t*>(A.grad) + n * A.ldg + k0), raw[u]);
                 }
             }
         }
+        float rs[G];
 #pragma unroll
         for (int u = 0; u < G; ++u) {
             const int i = i0 + u;
@@ -148,16 +170,27 @@ __global__ void __launch_bounds__(VH_THREADS) vhat_kernel(VhatArgs A) {
 #pragma unroll
                 for (int j = 0; j < 8; ++j) g2[j] = 0.0f;
             }
-            // row partial: lane sum of 8 columns, then xor butterfly
-            float s = g2[0];
+            // row partial: lane sum of 8 columns (the xor butterfly follows for
+            // the group's rows side by side)
+            float sr = g2[0];
 #pragma unroll
-            for (int j = 1; j < 8; ++j) s = s + g2[j];
-#pragma unroll
-            for (int o = 16; o >= 1; o >>= 1) s = s + __shfl_xor_sync(0xffffffffu, s, o);
-            if (lane == 0 && n < A.N) A.rp[(int64_t)cs * A.N + n] = s;
+            for (int j = 1; j < 8; ++j) sr = sr + g2[j];
+            rs[u] = sr;
             // column partial: this warp's rows in order
 #pragma unroll
             for (int j = 0; j < 8; ++j) cacc[j] = (i == 0) ? g2[j] : cacc[j] + g2[j];
+        }
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) {
+#pragma unroll
+            for (int u = 0; u < G; ++u) rs[u] = rs[u] + __shfl_xor_sync(0xffffffffu, rs[u], o);
+        }
+        if (lane == 0) {
+#pragma unroll
+            for (int u = 0; u < G; ++u) {
+                const int64_t n = (int64_t)rb * VH_ROWS + warp + 8 * (i0 + u);
+                if (n < A.N) A.rp[(int64_t)cs * A.N + n] = rs[u];
+            }
         }
     }
 #pragma unroll
@@ -170,83 +203,87 @@ __global__ void __launch_bounds__(VH_THREADS) vhat_kernel(VhatArgs A) {
         const int64_t col = (int64_t)cs * VH_COLS + threadIdx.x;
         if (col < A.K) A.cp[(int64_t)rb * A.K + col] = tot;
     }
-    __threadfence();
-    __syncthreads();
-    unsigned* cnt_rb = A.cnt;
-    unsigned* cnt_cs = A.cnt + A.nrb;
-    unsigned* cnt_g = A.cnt + A.nrb + A.ncs;
-    if (threadIdx.x == 0) {
-        flags[0] = atomicAdd(cnt_cs + cs, 1u) == (unsigned)(A.nrb - 1);
-        flags[1] = atomicAdd(cnt_rb + rb, 1u) == (unsigned)(A.ncs - 1);
+    __syncthreads();   // shared memory is reused by the next tile
     }
-    __syncthreads();
-    if (flags[0]) {  // last block of this column slab: finish v_col
-        __threadfence();
-        const int64_t col = (int64_t)cs * VH_COLS + threadIdx.x;
+}
+
+// Second launch: the fixed-order folds of the partials (the launch boundary
+// orders them after every tile).  Blocks [0, ncb): 256 columns each,
+// v_col (or the raw column sums) from the nrb column partials in row-block
+// order.  Blocks [ncb, ncb + nrf): 256 rows each, v_row from the ncs row
+// partials in slab order; the last of those blocks to finish sums v_row
+// (thread t: rows t, t+256, ...; then a tree over the 256 threads) into
+// sum_v_inv (or the raw sum).
+__global__ void __launch_bounds__(VH_THREADS) vhat_fold_kernel(VhatArgs A, int ncb, const int32_t* err) {
+    __shared__ float red[VH_THREADS];
+    __shared__ int last;
+    if (err && ld_volatile(err) != 0) return;   // the partials were not written
+    if ((int)blockIdx.x < ncb) {
+        const int64_t col = (int64_t)blockIdx.x * VH_THREADS + threadIdx.x;
         if (col < A.K) {
-            // fixed order b = 0, 1, ..., nrb-1; the loads of 8 partials go out together
+            // fixed order b = 0, 1, ..., nrb-1; the loads of 16 partials go out together
             float t = __ldcg(A.cp + col);
             int b = 1;
-            for (; b + 8 <= A.nrb; b += 8) {
-                float v[8];
+            for (; b + 16 <= A.nrb; b += 16) {
+                float v[16];
 #pragma unroll
-                for (int u = 0; u < 8; ++u) v[u] = __ldcg(A.cp + (int64_t)(b + u) * A.K + col);
+                for (int u = 0; u < 16; ++u) v[u] = __ldcg(A.cp + (int64_t)(b + u) * A.K + col);
 #pragma unroll
-                for (int u = 0; u < 8; ++u) t = t + v[u];
+                for (int u = 0; u < 16; ++u) t = t + v[u];
             }
             for (; b < A.nrb; ++b) t = t + __ldcg(A.cp + (int64_t)b * A.K + col);
             if (A.col_sum_out) A.col_sum_out[col] = t;
             else A.v_col[col] = A.b2 * A.v_col[col] + A.omb2 * t;
         }
-        if (threadIdx.x == 0) cnt_cs[cs] = 0;
+        return;
     }
-    if (flags[1]) {  // last block of this row block: finish v_row, maybe sum_v
-        __threadfence();
-        if (threadIdx.x < VH_ROWS) {
-            const int64_t n = (int64_t)rb * VH_ROWS + threadIdx.x;
-            if (n < A.N) {
-                float t = __ldcg(A.rp + n);
-                for (int c = 1; c < A.ncs; ++c) t = t + __ldcg(A.rp + (int64_t)c * A.N + n);
-                A.v_row[n] = A.b2 * A.v_row[n] + A.omb2 * t;
-            }
-        }
-        __threadfence();
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            cnt_rb[rb] = 0;
-            flags[0] = atomicAdd(cnt_g, 1u) == (unsigned)(A.nrb - 1);
-        }
-        __syncthreads();
-        if (flags[0]) {
-            __threadfence();
-            // fixed order n = t, t+256, t+512, ...; the loads of 8 go out together
-            float acc = 0.0f;
-            int64_t n = threadIdx.x;
-            for (; n + 7 * VH_THREADS < A.N; n += 8 * VH_THREADS) {
-                float v[8];
-#pragma unroll
-                for (int u = 0; u < 8; ++u) v[u] = __ldcg(A.v_row + n + u * VH_THREADS);
-#pragma unroll
-                for (int u = 0; u < 8; ++u) acc = acc + v[u];
-            }
-            for (; n < A.N; n += VH_THREADS) acc = acc + __ldcg(A.v_row + n);
-            red[threadIdx.x] = acc;
-            __syncthreads();
-            for (int s = VH_THREADS / 2; s >= 1; s >>= 1) {
-                if (threadIdx.x < s) red[threadIdx.x] = red[threadIdx.x] + red[threadIdx.x + s];
-                __syncthreads();
-            }
-            if (threadIdx.x == 0) {
-                if (A.vsum_out) {
-                    *A.vsum_out = red[0];
-                } else {
-                    float sv = np_max(red[0], 1e-30f);
-                    *A.sum_v_inv = 1.0f / sv;
-                }
-                *cnt_g = 0;
-            }
-        }
+    const int nrf = (int)gridDim.x - ncb;
+    const int64_t n = (int64_t)(blockIdx.x - ncb) * VH_THREADS + threadIdx.x;
+    if (n < A.N) {
+        float t = __ldcg(A.rp + n);
+        for (int c = 1; c < A.ncs; ++c) t = t + __ldcg(A.rp + (int64_t)c * A.N + n);
+        A.v_row[n] = A.b2 * A.v_row[n] + A.omb2 * t;
     }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        last = atomicAdd(A.cnt, 1u) == (unsigned)(nrf - 1);
+        __threadfence();
+    }
+    __syncthreads();
+    if (!last) return;
+    // fixed order n = t, t+256, t+512, ...; the loads of 8 go out together
+    float acc = 0.0f;
+    int64_t m = threadIdx.x;
+    for (; m + 7 * VH_THREADS < A.N; m += 8 * VH_THREADS) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = __ldcg(A.v_row + m + u * VH_THREADS);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) acc = acc + v[u];
+    }
+    for (; m < A.N; m += VH_THREADS) acc = acc + __ldcg(A.v_row + m);
+    red[threadIdx.x] = acc;
+    __syncthreads();
+    for (int s = VH_THREADS / 2; s >= 1; s >>= 1) {
+        if (threadIdx.x < s) red[threadIdx.x] = red[threadIdx.x] + red[threadIdx.x + s];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        if (A.vsum_out) {
+            *A.vsum_out = red[0];
+        } else {
+            float sv = np_max(red[0], 1e-30f);
+            *A.sum_v_inv = 1.0f / sv;
+        }
+        *A.cnt = 0;
+    }
+}
+
+static void vhat_fold(const VhatArgs& A, const int32_t* err, cudaStream_t st) {
+    const int ncb = (int)((A.K + VH_THREADS - 1) / VH_THREADS);
+    const int64_t nrf = A.N > 0 ? (A.N + VH_THREADS - 1) / VH_THREADS : 1;
+    vhat_fold_kernel<<<(unsigned)(ncb + nrf), VH_THREADS, 0, st>>>(A, ncb, err);
 }
 
 // shard mode, after the all-reduce of (column sums, v_row sum) over ranks
@@ -272,6 +309,18 @@ static void vhat_layout(int64_t N, int64_t K, int* ncs, int* nrb, size_t* off_rp
     *total = *off_cp + (size_t)(*nrb) * (size_t)K * sizeof(float);
 }
 
+// one block per tile up to VH_BLOCKS_PER_SM resident blocks on every SM
+static unsigned vhat_grid(int ncs, int nrb) {
+    static const int sms = [] {
+        int dev = 0, n = 148;
+        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        return n > 0 ? n : 148;
+    }();
+    const int64_t tiles = (int64_t)ncs * nrb;
+    const int64_t cap = (int64_t)sms * VH_BLOCKS_PER_SM;
+    return (unsigned)(tiles < cap ? tiles : cap);
+}
+
 extern "C" size_t concord_vhat_workspace_bytes(int64_t N, int64_t K) {
     if (N <= 0 || K <= 0) return 0;
     int ncs, nrb; size_t a, b, t;
@@ -288,15 +337,15 @@ static int vhat_launch(const uint16_t* grad, int64_t ldg, int64_t N, int64_t K, 
     vhat_layout(N, K, &ncs, &nrb, &off_rp, &off_cp, &total);
     if (!workspace || workspace_bytes < total)
         return fail(CONCORD_EWORKSPACE, std::string(name) + ": workspace smaller than concord_vhat_workspace_bytes(N, K)");
-    if (nrb > 65535) return fail(CONCORD_ETOOBIG, std::string(name) + ": too many rows for one launch");
+    if ((int64_t)ncs * nrb > INT32_MAX) return fail(CONCORD_ETOOBIG, std::string(name) + ": too many tiles for one launch");
     char* ws = static_cast<char*>(workspace);
     VhatArgs A{grad, ldg, N, K, v_row, v_col, sum_v_inv, beta2, one_minus_beta2, row_max, col_max, salt,
                reinterpret_cast<float*>(ws + off_rp), reinterpret_cast<float*>(ws + off_cp),
                reinterpret_cast<unsigned*>(ws), ncs, nrb,
                (K % 8 == 0) && (ldg % 8 == 0) && aligned(grad, 16), col_sum_out, vsum_out,
                nullptr, nullptr, 0, PeerSync{}};
-    dim3 grid((unsigned)ncs, (unsigned)nrb);
-    vhat_kernel<0><<<grid, VH_THREADS, 0, as_stream(stream)>>>(A);
+    vhat_kernel<0><<<vhat_grid(ncs, nrb), VH_THREADS, 0, as_stream(stream)>>>(A);
+    vhat_fold(A, nullptr, as_stream(stream));
     return check_launch(name);
 }
 
@@ -320,7 +369,7 @@ extern "C" int concord_vhat_partial(const uint16_t* grad, int64_t ldg, int64_t N
 }
 
 template <int P>
-static void launch_peer_vhat(dim3 grid, cudaStream_t st, const VhatArgs& A) {
+static void launch_peer_vhat(unsigned grid, cudaStream_t st, const VhatArgs& A) {
     vhat_kernel<P><<<grid, VH_THREADS, 0, st>>>(A);
 }
 
@@ -346,13 +395,13 @@ extern "C" int concord_peer_reduce_vhat(const uint16_t* own_rows, const uint16_t
     if (!workspace || workspace_bytes < total)
         return fail(CONCORD_EWORKSPACE, std::string(name) + ": workspace smaller than "
                                         "concord_vhat_workspace_bytes(max(n_rows, 1), K)");
-    if (nrb > 65535) return fail(CONCORD_ETOOBIG, std::string(name) + ": too many rows for one launch");
+    if ((int64_t)ncs * nrb > INT32_MAX) return fail(CONCORD_ETOOBIG, std::string(name) + ": too many tiles for one launch");
     char* ws = static_cast<char*>(workspace);
     VhatArgs A{grad_out, K, n_rows, K, v_row, nullptr, nullptr, beta2, one_minus_beta2, row_max, col_max, salt,
                reinterpret_cast<float*>(ws + off_rp), reinterpret_cast<float*>(ws + off_cp),
                reinterpret_cast<unsigned*>(ws), ncs, nrb, true, col_sum_out, vsum_out, own_rows, recv, S,
                PeerSync{sync->flags, sync->peer_flags, sync->state, sync->rank, sync->n_ranks, sync->timeout_ns}};
-    dim3 grid((unsigned)ncs, (unsigned)nrb);
+    const unsigned grid = vhat_grid(ncs, nrb);
     cudaStream_t st = as_stream(stream);
     switch (sync->n_ranks) {
         case 1: launch_peer_vhat<1>(grid, st, A); break;
@@ -364,6 +413,7 @@ extern "C" int concord_peer_reduce_vhat(const uint16_t* own_rows, const uint16_t
         case 7: launch_peer_vhat<7>(grid, st, A); break;
         default: launch_peer_vhat<8>(grid, st, A); break;
     }
+    vhat_fold(A, sync->state + 2, st);
     return check_launch(name);
 }
 
