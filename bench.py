@@ -164,14 +164,30 @@ def bench_ours(args, rank, world, device):
     for i in range(args.warmup):
         optimizer_step(layer, grads[i % 2])
     torch.cuda.synchronize()
-    # kernel timing pass (eager, CUDA events around the v-hat and step launches)
+    # kernel timing pass (eager, CUDA events around the v-hat and step launches;
+    # on N > 1 also after every phase of the peer transport)
     n_ev = min(args.steps, 200)
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(n_ev)]
+    names = ("push", "reduce_vhat", "allreduce_vhat", "allreduce_cmax")
+    use_ph = SHARDED is not None and SHARDED.peer is not None
+    phs = [{k: torch.cuda.Event(enable_timing=True) for k in names} for _ in range(n_ev)]
     for i in range(n_ev):
+        if use_ph:
+            SHARDED.phase_events = phs[i]
         optimizer_step(layer, grads[i % 2], ev=evs[i])
+    if use_ph:
+        SHARDED.phase_events = None
     torch.cuda.synchronize()
     step_kernel_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
     vhat_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    phases = None
+    if use_ph:
+        seq = [lambda i: evs[i][0], lambda i: phs[i]["push"], lambda i: phs[i]["reduce_vhat"],
+               lambda i: phs[i]["allreduce_vhat"], lambda i: evs[i][1], lambda i: evs[i][2],
+               lambda i: phs[i]["allreduce_cmax"]]
+        labels = ("push", "reduce_vhat", "allreduce_vhat", "vhat_finish", "step", "allreduce_cmax")
+        phases = {lab: statistics.mean(seq[j](i).elapsed_time(seq[j + 1](i)) for i in range(n_ev))
+                  for j, lab in enumerate(labels)}
     # the timed pass replays the step as CUDA graphs (one per gradient buffer):
     # the optimizer path has no host synchronisation, so it captures whole
     graphs = None
@@ -252,9 +268,13 @@ def bench_ours(args, rank, world, device):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, e2e_ms, step_kernel_ms = t.tolist()
+    if phases is not None:   # max over ranks, like every other multi-GPU time
+        pt = torch.tensor(list(phases.values()), device=device)
+        dist.all_reduce(pt, op=dist.ReduceOp.MAX)
+        phases = dict(zip(phases.keys(), pt.tolist()))
     return dict(ms=ms, e2e_ms=e2e_ms, step_kernel_ms=step_kernel_ms, vhat_ms=vhat_ms,
                 bytes_step=bytes_step, params=params, gemm_ms=gemm_ms, clocks=clk,
-                h2d=grads[0].numel() * 2, d2h=16, graphs=graphs is not None)
+                h2d=grads[0].numel() * 2, d2h=16, graphs=graphs is not None, phases=phases)
 
 
 def oracle_sample(rows, k_cols, seed=3):
@@ -393,6 +413,9 @@ def main():
                      "algorithmic_bytes_per_launch": shard_params * STEP_BYTES_PER_PARAM,
                      "kernel_ms": r["step_kernel_ms"]},
         "vhat_ms": r["vhat_ms"],
+        **({"dp_phases_ms": r["phases"],
+            "dp_phases_note": "eager pass, CUDA events between the peer transport's launches, "
+                              "mean over steps, max over ranks"} if r.get("phases") else {}),
         "cuda_graph": r["graphs"],
         "gemm": {k: {"ms": v, "tflops": flops / (v * 1e-3) / 1e12} for k, v in r["gemm_ms"].items()},
         "gemm_impl": "fwd/dx/dw: concord tcgen05 kernels (CUTLASS sm100 templates); cublas_*: torch",

@@ -26,25 +26,43 @@ constexpr int PEER_THREADS = 256;
 
 // Push half of the reduce-scatter: rows of rank q's shard [q*S, min(N, (q+1)*S))
 // of this rank's dW go to q's receive buffer, block `rank` (recv_q + rank*S*K),
-// for every q != rank, 16 bytes per thread and store.  Nothing waits: when
-// the last block has seen every block's stores fenced at system scope, it
-// announces the epoch to every rank.
-__global__ void __launch_bounds__(PEER_THREADS) peer_push_kernel(const uint4* grad, int64_t N, int64_t kc,
-                                                                 int64_t S, const uint64_t* recv, PeerSync s) {
+// for every q != rank, 16 bytes per load and store, four chunks in flight per
+// thread.  Nothing waits: when the last block has seen every block's stores
+// fenced at system scope, it announces the epoch to every rank.
+constexpr int PUSH_UNROLL = 4;
+
+template <typename I>   // index type: 32-bit when the whole gradient has < 2^31 chunks
+__device__ __forceinline__ void push_chunk(const uint4* grad, const uint64_t* recv, I c, I kc, I S, int rank,
+                                           uint4 v) {
+    const I n = c / kc;
+    const I q = n / S;
+    const int64_t dst = ((int64_t)rank * S + (n - q * S)) * (int64_t)kc + (c - n * kc);
+    __stcs(reinterpret_cast<uint4*>(recv[q]) + dst, v);
+}
+
+template <typename I>
+__global__ void __launch_bounds__(PEER_THREADS) peer_push_kernel(const uint4* grad, int64_t N, int64_t kc64,
+                                                                 int64_t S64, const uint64_t* recv, PeerSync s) {
     const int32_t e = ld_volatile(s.state) + 1;
     if (ld_volatile(s.state + 2) == 0) {
-        const int64_t total = N * kc;
-        const int64_t own0 = (int64_t)s.rank * S * kc, own1 = min(total, own0 + S * kc);
-        const int64_t stride = (int64_t)gridDim.x * PEER_THREADS;
-        for (int64_t c = (int64_t)blockIdx.x * PEER_THREADS + threadIdx.x; c < total; c += stride) {
-            if (c >= own0 && c < own1) {   // this rank's own rows stay where they are
-                c = own1 - 1 - ((own1 - 1 - c) % stride);   // jump to the last own chunk of this thread's lane
-                continue;
+        const I kc = (I)kc64, S = (I)S64;
+        const I total = (I)(N * kc64);
+        // this rank's own rows stay where they are: chunks [own0, own1) are skipped
+        const I own0 = (I)min((int64_t)total, (int64_t)s.rank * S64 * kc64);
+        const I own1 = (I)min((int64_t)total, ((int64_t)s.rank + 1) * S64 * kc64);
+        const I span = (I)gridDim.x * PEER_THREADS;
+        for (I c0 = (I)blockIdx.x * PEER_THREADS + threadIdx.x; c0 < total; c0 += span * PUSH_UNROLL) {
+            uint4 v[PUSH_UNROLL];
+            bool go[PUSH_UNROLL];
+#pragma unroll
+            for (int u = 0; u < PUSH_UNROLL; ++u) {
+                const I c = c0 + (I)u * span;
+                go[u] = c < total && (c < own0 || c >= own1);
+                if (go[u]) v[u] = __ldcs(grad + c);
             }
-            const int64_t n = c / kc;
-            const int64_t q = n / S;
-            const int64_t dst = ((int64_t)s.rank * S + (n - q * S)) * kc + (c - n * kc);
-            __stcs(reinterpret_cast<uint4*>(recv[q]) + dst, __ldcs(grad + c));
+#pragma unroll
+            for (int u = 0; u < PUSH_UNROLL; ++u)
+                if (go[u]) push_chunk<I>(grad, recv, c0 + (I)u * span, kc, S, s.rank, v[u]);
         }
     }
     __syncthreads();
@@ -180,7 +198,11 @@ extern "C" int concord_peer_push_rows(const uint16_t* grad, int64_t N, int64_t K
     int64_t blocks = (N * kc + PEER_THREADS - 1) / PEER_THREADS;
     if (blocks > 148 * 8) blocks = 148 * 8;
     if (blocks < 1) blocks = 1;
-    peer_push_kernel<<<(unsigned)blocks, PEER_THREADS, 0, as_stream(stream)>>>(
-        reinterpret_cast<const uint4*>(grad), N, kc, S, recv, s);
+    if (N * kc < ((int64_t)1 << 31) - (int64_t)blocks * PEER_THREADS * PUSH_UNROLL)
+        peer_push_kernel<uint32_t><<<(unsigned)blocks, PEER_THREADS, 0, as_stream(stream)>>>(
+            reinterpret_cast<const uint4*>(grad), N, kc, S, recv, s);
+    else
+        peer_push_kernel<int64_t><<<(unsigned)blocks, PEER_THREADS, 0, as_stream(stream)>>>(
+            reinterpret_cast<const uint4*>(grad), N, kc, S, recv, s);
     return check_launch("concord_peer_push_rows");
 }

@@ -282,6 +282,9 @@ class RowShardedStep:
         self.grad_shard = torch.empty(self.S, K, dtype=torch.bfloat16, device=dev)
         self.red = torch.zeros(K + 1, dtype=torch.float32, device=dev)
         self.step_events = None   # optional [_, start, end] CUDA events around the shard's step
+        # optional dict name -> CUDA event, recorded after each phase of the peer
+        # transport's step (instrumentation for the bench's phase breakdown)
+        self.phase_events = None
         self.peer = None
         if transport == "peer":
             wbuf, _, _ = layer._ensure_buffers()
@@ -321,13 +324,20 @@ class RowShardedStep:
             # one kernel waits for them and sums them in rank order together
             # with the shard's v-hat partials; the K+1 partials all-reduced
             # through the peer slots; v_col / sum_v_inv finished locally
+            ph = self.phase_events or {}
             grad_local = grad_local.contiguous()
             self.peer.push(grad_local)
+            if "push" in ph:
+                ph["push"].record()
             self.peer.reduce_vhat(grad_local[r0:r1], n_loc, self.grad_shard, L.v_row[r0:r1],
                                   L.adafactor_beta2, rmax[r0:r1] if track else None,
                                   cmax if track else None, kern.salt(L.packed_w.device),
                                   self.red[:K], self.red[K:])
+            if "reduce_vhat" in ph:
+                ph["reduce_vhat"].record()
             self.peer.allreduce(self.red, _abi.PEER_SUM_F32)
+            if "allreduce_vhat" in ph:
+                ph["allreduce_vhat"].record()
             kern.vhat_finish(self.red[:K], self.red[K:], L.v_col, L._sum_v_inv, L.adafactor_beta2)
             self._step_shard(params_of(L), n_loc, wbuf[r0:r1], rmax, cmax)
             # 4. column maxima through the peer slots.  The rendezvous inside
@@ -339,6 +349,8 @@ class RowShardedStep:
             # dW only after the v-hat all-reduce, i.e. after every rank finished
             # reading this one.
             self.peer.allreduce(cmax if track else None, _abi.PEER_MAX_I32)
+            if "allreduce_cmax" in ph:
+                ph["allreduce_cmax"].record()
             return
         # 1. reduce-scatter of the bf16 gradient over rows
         if self.even and grad_local.is_contiguous():
