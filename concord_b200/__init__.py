@@ -2,6 +2,7 @@
 
 Public API mirrors the reference's `concord` package (concord/__init__.py:7-31).
 """
+from .gated import GatedRebalance  # noqa: F401
 from .packed_b import (  # noqa: F401
     ConcordLinearPackedB,
     ConcordConv2dPackedB,
@@ -29,6 +30,7 @@ from .packed_b import (  # noqa: F401
 )
 
 __all__ = [
+    "GatedRebalance",
     "ConcordLinearPackedB",
     "ConcordConv2dPackedB",
     "compute_drift_cancel_C",

@@ -166,6 +166,10 @@ _SIGS = [
       ctypes.POINTER(PeerSync), _P]),
     ("concord_peer_allreduce", ctypes.c_int,
      [_P, _P, _I64, _I32, _P, _I64, ctypes.POINTER(PeerSync), _P]),
+    ("concord_rebalance_gated_layer_workspace_bytes", ctypes.c_size_t, [_I64, _I64]),
+    ("concord_rebalance_gated_layer_layout", ctypes.c_int, [_I64, _I64, _P, _P]),
+    ("concord_rebalance_gated", ctypes.c_int,
+     [_P, _I32, _I64, _P, _I64, _P, _I64, _I32, _P, _P, _P]),
     ("concord_rebalance_workspace_bytes", ctypes.c_size_t, [_I64, _I64]),
     ("concord_rebalance", ctypes.c_int,
      [_P, _I64, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32,

@@ -160,11 +160,166 @@ __global__ void reb_shift_kernel(RebArgs A) {
     }
 }
 
+// ---------------------------------------------------------------------------
+// Gated rebalance of many layers (the trainer-side GatedRebalance of the
+// reference, notebook/src/concord_winner.py:206-262): when ANY row or column
+// maximum of ANY layer exceeds max_m, every layer runs its rebalance (seed
+// bump, high-watermark fold, tick-up decisions, SR shift); otherwise none
+// does.  The reference decides on the host (one reduction and a device->host
+// read per step); here a gate launch writes the decision to device memory and
+// two batched launches cover every layer, predicated on it, so the whole
+// thing stays on the stream (graph-capturable) and costs three launches
+// whatever the number of layers.  Tick-down is not part of this path.
+// ---------------------------------------------------------------------------
+
+// gate[0] = 1 if any of the n values of maxima exceeds max_m
+__global__ void reb_gate_kernel(const int32_t* rows, int64_t nr, const int32_t* cols, int64_t nc,
+                                int32_t max_m, int32_t* gate) {
+    int hit = 0;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nr + nc;
+         i += (int64_t)gridDim.x * blockDim.x)
+        hit |= (i < nr ? rows[i] : cols[i - nr]) > max_m;
+    if (__syncthreads_or(hit) && threadIdx.x == 0) atomicOr(gate, 1);
+}
+
+__device__ __forceinline__ RebArgs reb_args_of(const concord_reb_layer& L) {
+    RebArgs A;
+    A.packed = L.packed; A.ldp = L.ldp; A.row_exp = L.row_exp; A.col_exp = L.col_exp;
+    A.row_max = L.row_max; A.col_max = L.col_max; A.row_hwm = L.row_hwm; A.col_hwm = L.col_hwm;
+    A.seed = L.seed; A.max_m = L.max_m; A.exp_max = L.exp_max; A.exp_min = L.exp_min; A.allow_td = 0;
+    A.N = L.N; A.K = L.K; A.row0 = L.row0; A.N_total = L.N_total; A.fired_out = nullptr;
+    A.rt = L.rt; A.ct = L.ct; A.fired = L.fired; A.rhist = nullptr; A.chist = nullptr;
+    A.rowlist = L.rowlist; A.collist = L.collist;
+    return A;
+}
+
+// one thread per row / column of every layer (layer l owns entries
+// [L.decide_off, L.decide_off + N + K)); layers found by binary search
+__global__ void reb_decide_many_kernel(const concord_reb_layer* layers, int32_t n_layers, int64_t total,
+                                       const int32_t* gate) {
+    if (*gate == 0) return;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        int lo = 0, hi = n_layers - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (layers[mid].decide_off <= i) lo = mid; else hi = mid - 1;
+        }
+        const concord_reb_layer& L = layers[lo];
+        const int64_t j = i - L.decide_off;
+        RebArgs A = reb_args_of(L);
+        if (j == 0) *A.seed += 1;
+        if (j < A.N) {
+            const int32_t mx = A.row_max[j];
+            if (A.row_hwm) A.row_hwm[j] = max(A.row_hwm[j], mx);
+            const int32_t e = A.row_exp[j];
+            const int t = mx > A.max_m && e < A.exp_max;
+            A.rt[j] = (int8_t)t;
+            if (t) {
+                A.row_exp[j] = (int8_t)(e + t);
+                atomicOr(A.fired, 1);
+                A.rowlist[atomicAdd(A.fired + 1, 1)] = (int32_t)j;
+            }
+        } else {
+            const int64_t k = j - A.N;
+            const int32_t mx = A.col_max[k];
+            if (A.col_hwm) A.col_hwm[k] = max(A.col_hwm[k], mx);
+            const int32_t e = A.col_exp[k];
+            const int t = mx > A.max_m && e < A.exp_max;
+            A.ct[k] = (int8_t)t;
+            if (t) {
+                A.col_exp[k] = (int8_t)(e + t);
+                atomicOr(A.fired, 1);
+                A.collist[atomicAdd(A.fired + 2, 1)] = (int32_t)k;
+            }
+        }
+    }
+}
+
+// every block walks the layers; a layer with nothing ticked costs one read.
+// Afterwards the per-layer counters are cleared for the next call (the last
+// block to finish clears them: the counters are read by every block).
+__global__ void reb_shift_many_kernel(const concord_reb_layer* layers, int32_t n_layers, const int32_t* gate,
+                                      int32_t* fired_out, uint32_t* done) {
+    if (*gate != 0) {
+        for (int l = 0; l < n_layers; ++l) {
+            const concord_reb_layer& L = layers[l];
+            const int32_t* f = L.fired;
+            if (f[0] == 0) continue;
+            RebArgs A = reb_args_of(L);
+            const int32_t sd = *A.seed;
+            const uint32_t NK = (uint32_t)(A.N_total * A.K);
+            const int64_t nr = f[1], nc = f[2];
+            const int64_t rows_work = nr * A.K, total = rows_work + A.N * nc;
+            for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+                 i += (int64_t)gridDim.x * blockDim.x) {
+                if (i < rows_work) {
+                    reb_shift_word(A, A.rowlist[i / A.K], i % A.K, sd, NK);
+                } else {
+                    const int64_t j = i - rows_work;
+                    const int64_t n = j / nc;
+                    if (A.rt[n] != 0) continue;
+                    reb_shift_word(A, n, A.collist[j % nc], sd, NK);
+                }
+            }
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(done, 1u) == gridDim.x - 1) {
+            if (fired_out) *fired_out = *gate;
+            for (int l = 0; l < n_layers; ++l) {
+                int32_t* f = layers[l].fired;
+                f[0] = 0; f[1] = 0; f[2] = 0;
+            }
+            *const_cast<int32_t*>(gate) = 0;
+            *done = 0;
+            __threadfence();
+        }
+    }
+}
+
 }  // namespace concord
 
 using namespace concord;
 
 static size_t al256(size_t x) { return (x + 255) / 256 * 256; }
+
+extern "C" size_t concord_rebalance_gated_layer_workspace_bytes(int64_t N, int64_t K) {
+    if (N <= 0 || K <= 0) return 0;
+    return 256 + al256((size_t)N) + al256((size_t)K) + al256((size_t)N * 4) + al256((size_t)K * 4);
+}
+
+extern "C" int concord_rebalance_gated_layer_layout(int64_t N, int64_t K, void* workspace, concord_reb_layer* layer) {
+    if (!workspace || !layer || N <= 0 || K <= 0) return fail(CONCORD_EINVAL, "concord_rebalance_gated_layer_layout: bad arguments");
+    char* ws = static_cast<char*>(workspace);
+    layer->fired = reinterpret_cast<int32_t*>(ws);
+    layer->rt = reinterpret_cast<int8_t*>(ws + 256);
+    layer->ct = reinterpret_cast<int8_t*>(ws + 256 + al256((size_t)N));
+    layer->rowlist = reinterpret_cast<int32_t*>(ws + 256 + al256((size_t)N) + al256((size_t)K));
+    layer->collist = reinterpret_cast<int32_t*>(ws + 256 + al256((size_t)N) + al256((size_t)K) + al256((size_t)N * 4));
+    return CONCORD_OK;
+}
+
+extern "C" int concord_rebalance_gated(const concord_reb_layer* layers, int32_t n_layers, int64_t total_decide,
+                                       const int32_t* row_max_all, int64_t n_rows_all, const int32_t* col_max_all,
+                                       int64_t n_cols_all, int32_t gate_max_m, int32_t* gate, int32_t* fired_out,
+                                       void* stream) {
+    if (!layers || !gate || n_layers <= 0 || total_decide <= 0 || !row_max_all || !col_max_all)
+        return fail(CONCORD_EINVAL, "concord_rebalance_gated: bad arguments");
+    cudaStream_t s = as_stream(stream);
+    int64_t gb = (n_rows_all + n_cols_all + RB_THREADS - 1) / RB_THREADS;
+    if (gb > 148 * 4) gb = 148 * 4;
+    reb_gate_kernel<<<(unsigned)(gb > 0 ? gb : 1), RB_THREADS, 0, s>>>(row_max_all, n_rows_all, col_max_all,
+                                                                      n_cols_all, gate_max_m, gate);
+    int64_t db = (total_decide + RB_THREADS - 1) / RB_THREADS;
+    if (db > 148 * 8) db = 148 * 8;
+    reb_decide_many_kernel<<<(unsigned)db, RB_THREADS, 0, s>>>(layers, n_layers, total_decide, gate);
+    reb_shift_many_kernel<<<148 * 4, RB_THREADS, 0, s>>>(layers, n_layers, gate, fired_out,
+                                                          reinterpret_cast<uint32_t*>(gate + 1));
+    return check_launch("concord_rebalance_gated");
+}
 
 extern "C" size_t concord_rebalance_workspace_bytes(int64_t N, int64_t K) {
     if (N <= 0 || K <= 0) return 0;

@@ -31,6 +31,8 @@
  *                            (packed_b.py:1129-1190, 959-1095) and the
  *                            high-watermark fold + seed bump of
  *                            ConcordLinearPackedB.rebalance (1792-1814)
+ *   concord_rebalance_gated <- GatedRebalance.__call__
+ *                            (notebook/src/concord_winner.py:206-262)
  *   concord_materialize   <- materialize_packed_bf16 (packed_b.py:120-170),
  *                            consolidated_weight (1632-1649)
  *   concord_quantize      <- ConcordLinearPackedB.load_weights (1570-1603),
@@ -217,6 +219,42 @@ int concord_step_sharded(const concord_step_params* p,
                          int64_t N, int64_t K, int64_t row0,
                          double* coh_stats, const uint64_t* wbuf_peers, int32_t n_peers,
                          void* stream);
+
+/*
+ * Gated rebalance of many layers (the trainer-side GatedRebalance of the
+ * reference, notebook/src/concord_winner.py:206-262): if any value of
+ * row_max_all[0..n_rows_all) or col_max_all[0..n_cols_all) (every layer's
+ * maxima, held in two shared arrays) exceeds gate_max_m, every layer runs
+ * its rebalance -- seed bump, high-watermark fold, tick-up decisions from
+ * the pre-launch exponents, SR shift of the ticked words (as
+ * concord_rebalance with allow_tickdown 0) -- otherwise none does.  The
+ * decision stays on the device: three launches, no host synchronisation.
+ * `layers` is a DEVICE array of n_layers descriptors; layer l's decide
+ * entries are [decide_off, decide_off + N + K) of [0, total_decide), in
+ * increasing order.  Each layer's rt/ct/fired/rowlist/collist point into a
+ * zero-filled workspace of concord_rebalance_gated_layer_workspace_bytes(N, K)
+ * bytes (concord_rebalance_gated_layer_layout fills those five fields).
+ * gate: device int32[2], zero-filled before the first call (the call leaves
+ * it zeroed).  fired_out (optional): 1 if the layers ran, else 0.
+ */
+typedef struct concord_reb_layer {
+    int32_t* packed; int64_t ldp;
+    int8_t* row_exp; int8_t* col_exp;
+    const int32_t* row_max; const int32_t* col_max;
+    int32_t* row_hwm; int32_t* col_hwm;      /* may be NULL */
+    int32_t* seed;
+    int32_t max_m, exp_max, exp_min, pad0;
+    int64_t N, K, row0, N_total;
+    int64_t decide_off;
+    int8_t* rt; int8_t* ct; int32_t* fired; int32_t* rowlist; int32_t* collist;
+} concord_reb_layer;
+
+size_t concord_rebalance_gated_layer_workspace_bytes(int64_t N, int64_t K);
+int concord_rebalance_gated_layer_layout(int64_t N, int64_t K, void* workspace, concord_reb_layer* layer);
+int concord_rebalance_gated(const concord_reb_layer* layers, int32_t n_layers, int64_t total_decide,
+                            const int32_t* row_max_all, int64_t n_rows_all, const int32_t* col_max_all,
+                            int64_t n_cols_all, int32_t gate_max_m, int32_t* gate, int32_t* fired_out,
+                            void* stream);
 
 /*
  * Peer memory for the data-parallel step over NVLink (no reference
