@@ -14,6 +14,10 @@ from .packed_b import (  # noqa: F401
     set_coh_weighted_v,
     set_ratio_coh,
     set_ratio_coh_floors,
+    set_ratio_floor_tensors,
+    set_consolidate,
+    set_sigmag_noise,
+    set_sigmag_sigma,
     reset_reb_stats,
     get_reb_stats,
     gate_coherence_from_fields,

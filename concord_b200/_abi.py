@@ -8,6 +8,7 @@ import ctypes
 import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
+ABI_VERSION = 2   # CONCORD_ABI_VERSION of include/concord_b200.h
 LIB_PATH = os.path.join(_HERE, "_lib", "libconcord_b200.so")
 
 # flag bits (packed_b.py:451-458 constexprs)
@@ -63,6 +64,8 @@ class StepParams(ctypes.Structure):
         ("leak_floor", ctypes.c_float),
         ("one_minus_leak_floor", ctypes.c_float),
         ("alpha_gate_gain", ctypes.c_float),
+        ("consolidate", ctypes.c_void_p),
+        ("ratio_floors", ctypes.c_void_p),
     ]
 
 
@@ -202,6 +205,9 @@ def load():
         fn = getattr(lib, name)
         fn.restype = res
         fn.argtypes = args
+    if lib.concord_abi_version() != ABI_VERSION:
+        raise RuntimeError(f"{LIB_PATH} has ABI version {lib.concord_abi_version()}, this package "
+                           f"needs {ABI_VERSION}: rebuild with `python -m concord_b200.build`")
     _LIB = lib
     return lib
 

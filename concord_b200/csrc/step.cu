@@ -21,6 +21,12 @@ namespace concord {
 struct StepScalars {
     float lr, eps, svi;
     int32_t salt;
+    // gradient accumulation (P.consolidate): consf multiplies the gated terms;
+    // emit == false freezes the weight and the row/col maxima
+    bool accum, emit;
+    float consf;
+    // ratio-coherence floors (P.ratio_floors overrides the launch values)
+    float chase_floor, om_chase_floor, leak_floor, om_leak_floor;
 };
 
 struct ElemOut {
@@ -136,8 +142,12 @@ __device__ __forceinline__ ElemOut adamw_post(const concord_step_params& P, cons
     } else {
         step_live = step_live + P.weight_decay * (d_fs * scale_fwd);
     }
-    float delta_t = -S.lr * step_live * scale_inv - P.beta1 * d_fs;
-    if (consol) delta_t = delta_t - evap;
+    // accumulation (dynamic flags only): the beta1 and evaporation terms are
+    // scaled by consf (prototype_packed_b.py:661); consf == 1 changes nothing
+    const bool accum = (FL & FL_DYNAMIC) && S.accum;
+    const float delta_grad = -S.lr * step_live * scale_inv;
+    float delta_t = accum ? delta_grad - S.consf * (P.beta1 * d_fs) : delta_grad - P.beta1 * d_fs;
+    if (consol) delta_t = accum ? delta_t - S.consf * evap : delta_t - evap;
 
     s_fast = s_fast + sr_tick(delta_t, hash_uniform(s_fast, pos, S.salt));
 
@@ -146,7 +156,7 @@ __device__ __forceinline__ ElemOut adamw_post(const concord_step_params& P, cons
     if (F & CONCORD_F_APPLY_CHASE) {
         float chase_mantissa;
         if (F & CONCORD_F_RATIO_COH) {
-            const float gate = P.chase_floor + P.one_minus_chase_floor * coh;
+            const float gate = S.chase_floor + S.om_chase_floor * coh;
             chase_mantissa = P.alpha * gate * P.gate_gain * (float)s_fast;
         } else if (F & CONCORD_F_COHPRE) {
             const float gate = coh + e.cp * (1.0f - coh);
@@ -156,13 +166,15 @@ __device__ __forceinline__ ElemOut adamw_post(const concord_step_params& P, cons
         } else {
             chase_mantissa = P.alpha_gate_gain * (float)s_fast;
         }
+        if (accum) chase_mantissa = chase_mantissa * S.consf;   // prototype_packed_b.py:695
         const int32_t ts = sr_tick(chase_mantissa / 128.0f, hash_uniform(s_fast, pos, S.salt ^ 0x5A5A5A5A));
         s_slow = s_slow + ts;
         s_fast = s_fast - ts * 128;
 
         float delta_v8 = P.alpha_v_fast * (float)(s_slow * 128 - v_slow * 128) / 128.0f;
+        if (accum) delta_v8 = delta_v8 * S.consf;                // prototype_packed_b.py:709
         if (F & CONCORD_F_RATIO_COH)
-            delta_v8 = delta_v8 * (P.leak_floor + P.one_minus_leak_floor * coh);
+            delta_v8 = delta_v8 * (S.leak_floor + S.om_leak_floor * coh);
         const int32_t tv = sr_tick(delta_v8, hash_uniform(s_fast, pos, S.salt ^ 0x33335555));
         new_v = clampi(v_slow + tv, -128, 127);
         if (F & CONCORD_F_MASS_PRESERVE) s_slow = s_slow - (new_v - v_slow);
@@ -170,11 +182,13 @@ __device__ __forceinline__ ElemOut adamw_post(const concord_step_params& P, cons
         const int32_t v_full_post = new_v * 128;
         const bool zero_wd = (FL & FL_ZERO_WD) != 0;
         if (!zero_wd && P.wd_sv != 0.0f) {  // a zero rate gives tick 0 for every finite state
-            const float d = S.lr * P.wd_sv * (float)(s_slow * 128 - v_full_post) / 128.0f;
+            float d = S.lr * P.wd_sv * (float)(s_slow * 128 - v_full_post) / 128.0f;
+            if (accum) d = d * S.consf;                          // prototype_packed_b.py:726
             s_slow = s_slow - sr_tick(d, hash_uniform(s_fast, pos, S.salt ^ 0x66665555));
         }
         if (!zero_wd && P.wd_sf != 0.0f) {
-            const float d = S.lr * P.wd_sf * (float)(s_slow * 128 + s_fast - v_full_post);
+            float d = S.lr * P.wd_sf * (float)(s_slow * 128 + s_fast - v_full_post);
+            if (accum) d = d * S.consf;                          // prototype_packed_b.py:737
             s_fast = s_fast - sr_tick(d, hash_uniform(s_fast, pos, S.salt ^ 0x77770000));
         }
     }
@@ -201,6 +215,7 @@ __device__ __forceinline__ void adamw_post_lockstep(const concord_step_params& P
     const uint32_t F = flags_of<FL>(P);
     const bool plain = (FL & FL_PLAIN) != 0;
     const bool consol = (F & CONCORD_F_GF_CONSOL) != 0;
+    const bool accum = (FL & FL_DYNAMIC) && S.accum;   // same gating as adamw_post
     int32_t sf[W], ss[W], nv[W];
     float cpn[W];
 #pragma unroll
@@ -211,8 +226,8 @@ __device__ __forceinline__ void adamw_post_lockstep(const concord_step_params& P
         if (consol) evap = S.lr * P.gf_consol * (1.0f - e[j].coh) * e[j].d_fs;
         else if (!plain) step_live = step_live + P.weight_decay * (e[j].d_fs * scale_fwd);
         float delta_t = -S.lr * step_live * scale_inv;
-        if (!plain) delta_t = delta_t - P.beta1 * e[j].d_fs;
-        if (consol) delta_t = delta_t - evap;
+        if (!plain) delta_t = accum ? delta_t - S.consf * (P.beta1 * e[j].d_fs) : delta_t - P.beta1 * e[j].d_fs;
+        if (consol) delta_t = accum ? delta_t - S.consf * evap : delta_t - evap;
         sf[j] = e[j].s_fast + sr_tick(delta_t, hash_uniform(e[j].s_fast, pos[j], S.salt));
         ss[j] = e[j].s_slow;
         nv[j] = e[j].v_slow;
@@ -224,7 +239,7 @@ __device__ __forceinline__ void adamw_post_lockstep(const concord_step_params& P
             const float coh = e[j].coh;
             float chase_mantissa;
             if (F & CONCORD_F_RATIO_COH) {
-                const float gate = P.chase_floor + P.one_minus_chase_floor * coh;
+                const float gate = S.chase_floor + S.om_chase_floor * coh;
                 chase_mantissa = P.alpha * gate * P.gate_gain * (float)sf[j];
             } else if (F & CONCORD_F_COHPRE) {
                 const float gate = coh + e[j].cp * (1.0f - coh);
@@ -233,6 +248,7 @@ __device__ __forceinline__ void adamw_post_lockstep(const concord_step_params& P
             } else {
                 chase_mantissa = P.alpha_gate_gain * (float)sf[j];
             }
+            if (accum) chase_mantissa = chase_mantissa * S.consf;
             const int32_t ts = sr_tick(chase_mantissa / 128.0f, hash_uniform(sf[j], pos[j], S.salt ^ 0x5A5A5A5A));
             ss[j] = ss[j] + ts;
             sf[j] = sf[j] - ts * 128;
@@ -241,8 +257,9 @@ __device__ __forceinline__ void adamw_post_lockstep(const concord_step_params& P
         for (int j = 0; j < W; ++j) {
             const int32_t v_slow = e[j].v_slow;
             float delta_v8 = P.alpha_v_fast * (float)(ss[j] * 128 - v_slow * 128) / 128.0f;
+            if (accum) delta_v8 = delta_v8 * S.consf;
             if (F & CONCORD_F_RATIO_COH)
-                delta_v8 = delta_v8 * (P.leak_floor + P.one_minus_leak_floor * e[j].coh);
+                delta_v8 = delta_v8 * (S.leak_floor + S.om_leak_floor * e[j].coh);
             const int32_t tv = sr_tick(delta_v8, hash_uniform(sf[j], pos[j], S.salt ^ 0x33335555));
             nv[j] = clampi(v_slow + tv, -128, 127);
             if (F & CONCORD_F_MASS_PRESERVE) ss[j] = ss[j] - (nv[j] - v_slow);
@@ -252,11 +269,13 @@ __device__ __forceinline__ void adamw_post_lockstep(const concord_step_params& P
             for (int j = 0; j < W; ++j) {
                 const int32_t v_full_post = nv[j] * 128;
                 if (P.wd_sv != 0.0f) {
-                    const float d = S.lr * P.wd_sv * (float)(ss[j] * 128 - v_full_post) / 128.0f;
+                    float d = S.lr * P.wd_sv * (float)(ss[j] * 128 - v_full_post) / 128.0f;
+                    if (accum) d = d * S.consf;
                     ss[j] = ss[j] - sr_tick(d, hash_uniform(sf[j], pos[j], S.salt ^ 0x66665555));
                 }
                 if (P.wd_sf != 0.0f) {
-                    const float d = S.lr * P.wd_sf * (float)(ss[j] * 128 + sf[j] - v_full_post);
+                    float d = S.lr * P.wd_sf * (float)(ss[j] * 128 + sf[j] - v_full_post);
+                    if (accum) d = d * S.consf;
                     sf[j] = sf[j] - sr_tick(d, hash_uniform(sf[j], pos[j], S.salt ^ 0x77770000));
                 }
             }
@@ -353,6 +372,21 @@ __device__ __forceinline__ StepScalars load_scalars(const StepArgs& A) {
     S.salt = *A.salt;
     const bool need_vhat = (A.P.flags & (CONCORD_F_GF_TRUST | CONCORD_F_GF_CONSOL | CONCORD_F_COHPRE | CONCORD_F_RATIO_COH)) != 0;
     S.svi = (need_vhat && A.P.kind == CONCORD_KIND_ADAMW) ? *A.sum_v_inv : 0.0f;
+    S.accum = A.P.consolidate != nullptr && A.P.kind == CONCORD_KIND_ADAMW;
+    const int32_t cons = S.accum ? *A.P.consolidate : 1;
+    S.consf = (float)cons;
+    S.emit = cons == 1;
+    if (A.P.ratio_floors) {
+        S.chase_floor = A.P.ratio_floors[0];
+        S.om_chase_floor = 1.0f - S.chase_floor;
+        S.leak_floor = A.P.ratio_floors[1];
+        S.om_leak_floor = 1.0f - S.leak_floor;
+    } else {
+        S.chase_floor = A.P.chase_floor;
+        S.om_chase_floor = A.P.one_minus_chase_floor;
+        S.leak_floor = A.P.leak_floor;
+        S.om_leak_floor = A.P.one_minus_leak_floor;
+    }
     return S;
 }
 
@@ -410,6 +444,8 @@ __global__ void __launch_bounds__(STEP_THREADS, MINB) step_vec_kernel(StepArgs A
     // peer rows start on 16 bytes when the row stride is a multiple of 8 elements
     // (peer buffers are whole allocations, so their bases are aligned)
     const bool peer16 = (A.ldw % 8) == 0;
+    // accumulation micro-step (P.consolidate != 1): the weight and the maxima stay frozen
+    const bool emit = !(FL & FL_DYNAMIC) || S.emit;
 
     int32_t ce[VEC];
     float vc[VEC];
@@ -509,8 +545,10 @@ __global__ void __launch_bounds__(STEP_THREADS, MINB) step_vec_kernel(StepArgs A
                 wv[j] = o.word;
                 cp[j] = o.coh_pre;
                 wf[j] = o.wval;
-                rml = max(rml, o.abs_eff);
-                cmx[j] = max(cmx[j], o.abs_eff);
+                if (emit) {
+                    rml = max(rml, o.abs_eff);
+                    cmx[j] = max(cmx[j], o.abs_eff);
+                }
                 if (need_coh) csum += o.coh;
             }
             if (need_coh) ccnt += VEC;
@@ -518,10 +556,10 @@ __global__ void __launch_bounds__(STEP_THREADS, MINB) step_vec_kernel(StepArgs A
             __nv_bfloat162 b01 = __floats2bfloat162_rn(wf[0], wf[1]);
             __nv_bfloat162 b23 = __floats2bfloat162_rn(wf[2], wf[3]);
             wb = make_uint2(*reinterpret_cast<uint32_t*>(&b01), *reinterpret_cast<uint32_t*>(&b23));
-            __stcs(reinterpret_cast<uint2*>(A.wbuf + n * A.ldw + k0), wb);
+            if (emit) __stcs(reinterpret_cast<uint2*>(A.wbuf + n * A.ldw + k0), wb);
             if (write_cp) __stcs(reinterpret_cast<float4*>(pc), make_float4(cp[0], cp[1], cp[2], cp[3]));
         }
-        if (A.npeers > 0) {
+        if (A.npeers > 0 && emit) {
             // the all-gather of the forward weight: this row's weights into every
             // other rank's buffer, 16 bytes per even lane (its 4 columns and its
             // odd neighbour's), 8 bytes where the neighbour has no columns or the
@@ -582,16 +620,17 @@ __global__ void __launch_bounds__(STEP_THREADS) step_generic_kernel(StepArgs A) 
                                                 need_vhat ? A.v_row[n] : 0.0f, need_vhat ? A.v_col[k] : 0.0f,
                                                 cp, S, pos);
         A.packed[n * A.ldp + k] = o.word;
+        if (write_cp) A.coh_pre[n * A.ldc + k] = o.coh_pre;
+        if (need_coh) { csum += (double)o.coh; ccnt += 1.0; }
+        if (!S.emit) continue;   // accumulation micro-step: weight and maxima frozen
         const uint16_t wb = __bfloat16_as_ushort(__float2bfloat16_rn(o.wval));
         A.wbuf[n * A.ldw + k] = wb;
         for (int q = 0; q < A.npeers; ++q)
             reinterpret_cast<uint16_t*>(A.wpeers[q])[(A.row0 + n) * A.ldw + k] = wb;
-        if (write_cp) A.coh_pre[n * A.ldc + k] = o.coh_pre;
         if (track && o.abs_eff > 0) {
             atomicMax(A.row_max + n, o.abs_eff);
             atomicMax(A.col_max + k, o.abs_eff);
         }
-        if (need_coh) { csum += (double)o.coh; ccnt += 1.0; }
     }
     if (need_coh && A.coh_stats) block_add_coh(csum, ccnt, A.coh_stats);
 }
@@ -601,7 +640,9 @@ static void launch_vec(bool adamw, uint32_t F, bool has_cp, dim3 grid, cudaStrea
     const bool zero_wd = A.P.wd_sv == 0.0f && A.P.wd_sf == 0.0f && A.P.weight_decay == 0.0f &&
                          A.P.beta1 == 0.0f && A.P.v_scale == 0.0f && A.P.gf_trust_delta_sq == 1.0f &&
                          A.P.gate_gain == 1.0f && fabsf(A.P.drift_cancel_C) <= 1.0f;
+    const bool runtime_scalars = A.P.consolidate != nullptr || A.P.ratio_floors != nullptr;
     if (!adamw) step_vec_kernel<CONCORD_KIND_SGD, FL_DYNAMIC, MINB><<<grid, STEP_THREADS, 0, s>>>(A);
+    else if (runtime_scalars) step_vec_kernel<CONCORD_KIND_ADAMW, FL_DYNAMIC, MINB><<<grid, STEP_THREADS, 0, s>>>(A);
     else if (F == (FL_BARE & 0xffffu) && has_cp && zero_wd) step_vec_kernel<CONCORD_KIND_ADAMW, FL_BARE, MINB><<<grid, STEP_THREADS, 0, s>>>(A);
     else if (F == (FL_NOCOHPRE & 0xffffu) && zero_wd) step_vec_kernel<CONCORD_KIND_ADAMW, FL_NOCOHPRE, MINB><<<grid, STEP_THREADS, 0, s>>>(A);
     else step_vec_kernel<CONCORD_KIND_ADAMW, FL_DYNAMIC, MINB><<<grid, STEP_THREADS, 0, s>>>(A);

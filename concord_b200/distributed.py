@@ -227,7 +227,7 @@ def params_of(L):
         drift_cancel_C=L.drift_cancel_C, alpha_v_fast=L.alpha_v_fast, wd_sv=L.wd_sv,
         wd_sf=L.wd_sf, mass_preserve=L.mass_preserve_v, apply_chase=L.apply_chase,
         track_rebalance=L.track_rebalance, gf_trust_delta_sq=L.gf_trust_delta_sq,
-        use_cohpre=L._coh_pre is not None, mantissa_bias=L.MANTISSA_BIAS)
+        use_cohpre=L._coh_pre is not None, mantissa_bias=L.MANTISSA_BIAS, device=L.packed_w.device)
 
 
 def _reduce_scatter(out, inp, group):

@@ -76,6 +76,9 @@ def set_ratio_coh_floors(chase, leak):
     global _RATIO_CHASE_FLOOR, _RATIO_LEAK_FLOOR
     _RATIO_CHASE_FLOOR = float(chase)
     _RATIO_LEAK_FLOOR = float(leak)
+    for t in _FLOOR_TENSORS.values():   # device copies, read by captured graphs
+        t[0] = _RATIO_CHASE_FLOOR
+        t[1] = _RATIO_LEAK_FLOOR
 
 
 _REB_STATS = None
@@ -227,11 +230,14 @@ def adamw_params(alpha=0.1, beta1=0.0, weight_decay=0.0, step_cap=10.0, v_scale=
                  precond_p=0.5, gf_consol=0.0, drift_cancel_C=None, alpha_v_fast=0.001,
                  wd_sv=0.0, wd_sf=0.0, mass_preserve=False, apply_chase=True,
                  track_rebalance=True, gf_trust_delta_sq=0.0, use_cohpre=False,
-                 mantissa_bias=15):
-    """Launch scalars of the AdamW path with the module switches read now."""
+                 mantissa_bias=15, device=None):
+    """Launch scalars of the AdamW path with the module switches read now.
+    With `device`, the device scalars in use on it are attached: the
+    gradient-accumulation flag once set_consolidate() has been called there,
+    the ratio-floor tensors once set_ratio_floor_tensors(True)."""
     if drift_cancel_C is None:
         drift_cancel_C = compute_drift_cancel_C(alpha, alpha_v_fast, mass_preserve=mass_preserve)
-    return _abi.make_step_params(
+    p = _abi.make_step_params(
         kind="adamw", mantissa_bias=mantissa_bias, alpha=alpha, beta1=beta1,
         weight_decay=weight_decay, step_cap=step_cap, v_scale=v_scale, precond_p=precond_p,
         gf_consol=gf_consol, drift_cancel_C=drift_cancel_C, alpha_v_fast=alpha_v_fast,
@@ -239,6 +245,104 @@ def adamw_params(alpha=0.1, beta1=0.0, weight_decay=0.0, step_cap=10.0, v_scale=
         chase_floor=_RATIO_CHASE_FLOOR, leak_floor=_RATIO_LEAK_FLOOR,
         mass_preserve=mass_preserve, apply_chase=apply_chase, track_rebalance=track_rebalance,
         use_cohpre=use_cohpre, fixed_coh=_USE_FIXED_COH, ratio_coh=_RATIO_COH)
+    if device is not None:
+        key = _dev_key(device)
+        if key in _CONSOLIDATE_FLAGS:
+            p.consolidate = _CONSOLIDATE_FLAGS[key].data_ptr()
+        if _FLOOR_TENSORS_ON:
+            p.ratio_floors = _ensure_floor_tensors(device).data_ptr()
+    return p
+
+
+# ---- centered Sigma_g-shaped gradient noise (prototype_packed_b.py:881-915, 1477-1501) ----
+# EXPERIMENTAL in the reference and off by default: adds a draw shaped like the
+# per-token gradient covariance, mean-subtracted,
+#   noise = sum_i eps_i (g_i - gbar) = (eps * grad_y)^T x - (sum eps) gbar,  eps ~ N(0, 1),
+# scaled to sigma * ||grad_W|| (isotropic white noise of the same norm as an
+# ablation).  sigma is a device scalar, so a captured graph follows its schedule.
+_SIGMAG_NOISE = False
+_SIGMAG_ISO = False
+_SIGMAG_SIGMA = 0.0
+_SIGMAG_TENSORS = {}
+
+
+def set_sigmag_noise(enabled, isotropic=False):
+    global _SIGMAG_NOISE, _SIGMAG_ISO
+    _SIGMAG_NOISE = bool(enabled)
+    _SIGMAG_ISO = bool(isotropic)
+
+
+def set_sigmag_sigma(sigma):
+    global _SIGMAG_SIGMA
+    _SIGMAG_SIGMA = float(sigma)
+    for t in _SIGMAG_TENSORS.values():
+        t.fill_(_SIGMAG_SIGMA)
+
+
+def _get_sigmag_sigma(device):
+    key = _dev_key(device)
+    if key not in _SIGMAG_TENSORS:
+        _SIGMAG_TENSORS[key] = torch.full((1,), _SIGMAG_SIGMA, dtype=torch.float32, device=device)
+    return _SIGMAG_TENSORS[key]
+
+
+@torch.no_grad()
+def sigmag_noise(grad_W, grad_y_flat, x_flat):
+    """grad_W plus the centered Sigma_g-shaped noise (torch ops, in the
+    reference's order); returns bf16."""
+    gwf = grad_W.float()
+    if _SIGMAG_ISO:
+        noise = torch.randn_like(gwf)
+    else:
+        gyf = grad_y_flat.float()
+        M = gyf.shape[0]
+        e = torch.randn(M, device=gyf.device, dtype=torch.float32)
+        gbar = gwf / max(M, 1)
+        noise = (e[:, None] * gyf).transpose(0, 1) @ x_flat.float() - e.sum() * gbar
+    sig_t = _get_sigmag_sigma(gwf.device)
+    nrm = noise.norm().clamp_min(1e-12)
+    return (gwf + noise * (sig_t * gwf.norm() / nrm)).to(torch.bfloat16).contiguous()
+
+
+# ---- gradient accumulation and device-tensor schedules (prototype_packed_b.py:325-353, 1000-1010) ----
+_CONSOLIDATE_FLAGS = {}
+_FLOOR_TENSORS = {}
+_FLOOR_TENSORS_ON = False
+
+
+def _get_consolidate_flag(device):
+    key = _dev_key(device)
+    if key not in _CONSOLIDATE_FLAGS:
+        _CONSOLIDATE_FLAGS[key] = torch.ones(1, dtype=torch.int32, device=device)
+    return _CONSOLIDATE_FLAGS[key]
+
+
+def set_consolidate(device, consolidate: bool):
+    """Trainer hook for gradient accumulation: with False the next backward(s)
+    only SR-tick this micro-batch's gradient into s_fast (weight, slow
+    accumulators and rebalance maxima stay frozen); with True the step
+    consolidates as usual.  In a cycle of N micro-steps call False for the
+    first N-1 and True for the last.  An in-place fill of a device flag, so a
+    captured CUDA graph follows it.  The first call routes this device's AdamW
+    steps through the kernel variant that reads the flag."""
+    _get_consolidate_flag(device).fill_(1 if consolidate else 0)
+
+
+def _ensure_floor_tensors(device):
+    key = _dev_key(device)
+    if key not in _FLOOR_TENSORS:
+        _FLOOR_TENSORS[key] = torch.tensor([_RATIO_CHASE_FLOOR, _RATIO_LEAK_FLOOR], dtype=torch.float32,
+                                           device=device)
+    return _FLOOR_TENSORS[key]
+
+
+def set_ratio_floor_tensors(enabled):
+    """Read the ratio-coherence floors from device tensors (so a per-step
+    schedule set with set_ratio_coh_floors reaches a captured CUDA graph), as
+    the reference's prototype kernel does; 1 - floor is then computed in fp32
+    in the kernel, not in double on the host."""
+    global _FLOOR_TENSORS_ON
+    _FLOOR_TENSORS_ON = bool(enabled)
 
 
 def apply_packed_adamw(packed_w, grad_W, weight_buf, row_exp, col_exp, row_max, col_max,
@@ -268,7 +372,7 @@ def apply_packed_adamw(packed_w, grad_W, weight_buf, row_exp, col_exp, row_max, 
                           drift_cancel_C=drift_cancel_C, alpha_v_fast=alpha_v_fast, wd_sv=wd_sv,
                           wd_sf=wd_sf, mass_preserve=mass_preserve, apply_chase=apply_chase,
                           track_rebalance=track_rebalance, gf_trust_delta_sq=gf_trust_delta_sq,
-                          use_cohpre=use_cohpre, mantissa_bias=mantissa_bias)
+                          use_cohpre=use_cohpre, mantissa_bias=mantissa_bias, device=packed_w.device)
     salt = _get_step_counter(packed_w.device)
     if bump_salt:
         _salt_bump(salt)
@@ -473,6 +577,8 @@ class FusedConcordLinearPackedB(torch.autograd.Function):
         x_flat = x.reshape(-1, in_features)
         grad_y_flat = grad_y.reshape(-1, out_features)
         grad_W = _gemm.grad_weight(grad_y_flat, x_flat)
+        if _SIGMAG_NOISE:
+            grad_W = sigmag_noise(grad_W, grad_y_flat, x_flat)
         _packed_backward_step(ctx, grad_W)
         grad_bias = grad_y_flat.sum(0) if ctx.has_bias else None
         return (grad_x, None, None, None, grad_bias) + (None,) * 29

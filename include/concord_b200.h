@@ -54,7 +54,7 @@
 extern "C" {
 #endif
 
-#define CONCORD_ABI_VERSION 1
+#define CONCORD_ABI_VERSION 2
 
 /* status codes */
 #define CONCORD_OK            0
@@ -110,6 +110,23 @@ typedef struct concord_step_params {
     float leak_floor;
     float one_minus_leak_floor;     /* fp32(1.0 - leak_floor) */
     float alpha_gate_gain;          /* fp32(alpha * 1.0 * gate_gain): chase gain when no gate tensor */
+    /*
+     * Optional device scalars, read by the kernel at run time (so a captured
+     * CUDA graph follows their current values); NULL = not used.
+     *   consolidate: gradient accumulation gate of the reference's prototype
+     *     kernel (notebook/src/prototype_packed_b.py:481-515, 661-780).  The
+     *     SR tick of s_fast always applies; the beta1 and evaporation terms of
+     *     the tick, the chase, the v_slow leak and both weight decays are
+     *     multiplied by float(*consolidate); the bf16 weight and the row/col
+     *     maxima are written only when *consolidate == 1 (the weight stays
+     *     frozen during accumulation).  coh_pre is updated either way.
+     *     AdamW only.
+     *   ratio_floors: [chase_floor, leak_floor] for the ratio-coherence gate,
+     *     replacing chase_floor / leak_floor and their one_minus_* (then
+     *     1 - floor in fp32, as the prototype kernel computes it).
+     */
+    const int32_t* consolidate;
+    const float* ratio_floors;
 } concord_step_params;
 
 int         concord_abi_version(void);

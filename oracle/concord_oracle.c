@@ -168,18 +168,27 @@ static int32_t step_adamw_elem(const concord_step_params* P, int32_t packed, flo
     } else {
         step_live = step_live + P->weight_decay * s_fast_in_w;
     }
+    /* gradient-accumulation gate (prototype_packed_b.py:514-515, 661): the
+     * beta1 and evaporation terms only on the consolidate step */
+    const int accum = P->consolidate != NULL;
+    const float consf = accum ? (float)*P->consolidate : 1.0f;
     float delta_grad = -lr * step_live * scale_inv;
-    float delta_t = delta_grad - P->beta1 * d_fs;
-    if (consol) delta_t = delta_t - evap;
+    float delta_t = accum ? delta_grad - consf * (P->beta1 * d_fs) : delta_grad - P->beta1 * d_fs;
+    if (consol) delta_t = accum ? delta_t - consf * evap : delta_t - evap;
 
     float r1 = oracle_hash_uniform(s_fast, pos, salt);
     s_fast = s_fast + sr_tick(delta_t, r1);
 
+    /* ratio floors from device scalars: 1 - floor in fp32 (prototype_packed_b.py:510-511, 691) */
+    const float chase_floor = P->ratio_floors ? P->ratio_floors[0] : P->chase_floor;
+    const float om_chase_floor = P->ratio_floors ? 1.0f - P->ratio_floors[0] : P->one_minus_chase_floor;
+    const float leak_floor = P->ratio_floors ? P->ratio_floors[1] : P->leak_floor;
+    const float om_leak_floor = P->ratio_floors ? 1.0f - P->ratio_floors[1] : P->one_minus_leak_floor;
     int32_t new_v = v_slow;
     if (F & CONCORD_F_APPLY_CHASE) {
         float chase_mantissa;
         if (F & CONCORD_F_RATIO_COH) {
-            float gate = P->chase_floor + P->one_minus_chase_floor * coh;
+            float gate = chase_floor + om_chase_floor * coh;
             chase_mantissa = P->alpha * gate * P->gate_gain * (float)s_fast;
         } else if (F & CONCORD_F_COHPRE) {
             float cp = *coh_pre_io;
@@ -189,6 +198,7 @@ static int32_t step_adamw_elem(const concord_step_params* P, int32_t packed, flo
         } else {
             chase_mantissa = P->alpha_gate_gain * (float)s_fast;
         }
+        if (accum) chase_mantissa = chase_mantissa * consf;   /* prototype_packed_b.py:695 */
         float chase_i8 = chase_mantissa / 128.0f;
         float r2 = oracle_hash_uniform(s_fast, pos, salt ^ 0x5A5A5A5A);
         int32_t ts = sr_tick(chase_i8, r2);
@@ -197,8 +207,9 @@ static int32_t step_adamw_elem(const concord_step_params* P, int32_t packed, flo
 
         float gap = (float)(s_slow * 128 - v_slow_full);
         float delta_v8 = P->alpha_v_fast * gap / 128.0f;
+        if (accum) delta_v8 = delta_v8 * consf;                 /* prototype_packed_b.py:709 */
         if (F & CONCORD_F_RATIO_COH)
-            delta_v8 = delta_v8 * (P->leak_floor + P->one_minus_leak_floor * coh);
+            delta_v8 = delta_v8 * (leak_floor + om_leak_floor * coh);
         float r3 = oracle_hash_uniform(s_fast, pos, salt ^ 0x33335555);
         int32_t tv = sr_tick(delta_v8, r3);
         new_v = clampi(v_slow + tv, -128, 127);
@@ -207,12 +218,14 @@ static int32_t step_adamw_elem(const concord_step_params* P, int32_t packed, flo
         int32_t v_full_post = new_v * 128;
         float dsv_post = (float)(s_slow * 128 - v_full_post);
         float wd_sv_d = lr * P->wd_sv * dsv_post / 128.0f;
+        if (accum) wd_sv_d = wd_sv_d * consf;                   /* prototype_packed_b.py:726 */
         float r4 = oracle_hash_uniform(s_fast, pos, salt ^ 0x66665555);
         s_slow = s_slow - sr_tick(wd_sv_d, r4);
 
         int32_t sfl = s_slow * 128 + s_fast;
         float dsf = (float)(sfl - v_full_post);
         float wd_sf_d = lr * P->wd_sf * dsf;
+        if (accum) wd_sf_d = wd_sf_d * consf;                   /* prototype_packed_b.py:737 */
         float r5 = oracle_hash_uniform(s_fast, pos, salt ^ 0x77770000);
         s_fast = s_fast - sr_tick(wd_sf_d, r5);
     }
@@ -297,6 +310,9 @@ void oracle_step(const concord_step_params* P, int32_t* packed, int64_t ldp,
                 if (write_cp) coh_pre[n * ldc + k] = cp;
             }
             packed[n * ldp + k] = nw;
+            /* weight emit and maxima only on the consolidate step (prototype_packed_b.py:761-782) */
+            const int emit = P->kind == CONCORD_KIND_SGD || !P->consolidate || *P->consolidate == 1;
+            if (!emit) { if (coh == coh) { csum += coh; ccnt += 1.0; } continue; }
             wbuf[n * ldw + k] = wb;
             if (track) {
                 if (ae > row_max[n]) row_max[n] = ae;

@@ -32,7 +32,7 @@ def test_library_exports_header_symbols(built):
     assert declared == exported
     assert declared == set(_abi.EXPORTED)
     _abi.load()
-    assert _abi.load().concord_abi_version() == 1
+    assert _abi.load().concord_abi_version() == 2
 
 
 def test_crmath_host_matches_extended_precision(built):
