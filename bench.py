@@ -151,6 +151,43 @@ def optimizer_step(layer, grad, coh_stats=None, ev=None):
         layer.rebalance()
 
 
+def kernel_times(layer, grad, reps):
+    """Mean duration of the packed-step launch and of the v-hat launches, each
+    captured alone in a CUDA graph and replayed `reps` times between events."""
+    from concord_b200 import packed_b as pb
+    from concord_b200.distributed import params_of
+    wbuf, rmax, cmax = layer._ensure_buffers()
+    P = params_of(layer)
+    salt = pb._get_step_counter(layer.packed_w.device)
+
+    def step_only():
+        pb._step_launch(P, layer.packed_w, grad, wbuf, layer.row_exp, layer.col_exp, rmax, cmax,
+                        layer.v_row, layer.v_col, layer._sum_v_inv, layer._coh_pre, layer._lr_buf,
+                        layer._eps_buf, salt)
+
+    def vhat_only():
+        pb.vhat_update(grad, layer.v_row, layer.v_col, layer._sum_v_inv, layer.adafactor_beta2,
+                       row_max=rmax, col_max=cmax, bump_salt=True)
+
+    out = []
+    for fn in (step_only, vhat_only):
+        fn()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        g.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        out.append(a.elapsed_time(b) / reps)
+    return tuple(out)
+
+
 def bench_ours(args, rank, world, device):
     global SHARDED
     n_rows, k_cols = args.rows, args.cols
@@ -180,6 +217,11 @@ def bench_ours(args, rank, world, device):
     torch.cuda.synchronize()
     step_kernel_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
     vhat_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    if world == 1 and args.graph:
+        # the eager events above include host gaps when a launch is shorter than
+        # its Python: time the step and v-hat launches as back-to-back replays of
+        # one-launch CUDA graphs instead (the roofline's kernel time)
+        step_kernel_ms, vhat_ms = kernel_times(layer, grads[0], reps=min(args.steps, 50))
     phases = None
     if use_ph:
         seq = [lambda i: evs[i][0], lambda i: phs[i]["push"], lambda i: phs[i]["reduce_vhat"],

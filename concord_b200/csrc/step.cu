@@ -363,6 +363,7 @@ struct StepArgs {
     double* coh_stats;
     const uint64_t* wpeers;  // other ranks' full forward-weight buffers (row stride ldw), or null
     int32_t npeers;
+    int32_t rows_per_block;  // vector kernel: rows of one block (a multiple of 8)
 };
 
 __device__ __forceinline__ StepScalars load_scalars(const StepArgs& A) {
@@ -398,7 +399,7 @@ namespace concord {
 constexpr int STEP_THREADS = 256;
 constexpr int VEC = 4;                 // consecutive columns per thread
 constexpr int STEP_COLS = 32 * VEC;    // columns per block (one warp-width)
-constexpr int STEP_ROWS = 64;          // rows per block (8 per warp)
+constexpr int STEP_ROWS = 64;          // rows per block (8 per warp); fewer on small layers
 
 __device__ __forceinline__ void block_add_coh(double csum, double ccnt, double* coh_stats) {
     __shared__ double red[2][STEP_THREADS / 32];
@@ -432,7 +433,8 @@ __global__ void __launch_bounds__(STEP_THREADS, MINB) step_vec_kernel(StepArgs A
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int64_t k0 = (int64_t)blockIdx.x * STEP_COLS + lane * VEC;
     const bool active = k0 < A.K;
-    const int64_t rbase = (int64_t)blockIdx.y * STEP_ROWS;
+    const int rows_pb = A.rows_per_block;
+    const int64_t rbase = (int64_t)blockIdx.y * rows_pb;
     const uint32_t F = flags_of<FL>(A.P);
     const bool adamw = KIND == CONCORD_KIND_ADAMW;
     const bool need_vhat = adamw && (F & (CONCORD_F_GF_TRUST | CONCORD_F_GF_CONSOL | CONCORD_F_COHPRE | CONCORD_F_RATIO_COH));
@@ -483,7 +485,7 @@ __global__ void __launch_bounds__(STEP_THREADS, MINB) step_vec_kernel(StepArgs A
         }
     };
     prefetch(rbase + warp);
-    for (int r = warp; r < STEP_ROWS; r += STEP_THREADS / 32) {
+    for (int r = warp; r < rows_pb; r += STEP_THREADS / 32) {
         const int64_t n = rbase + r;
         if (n >= A.N) break;
         int rml = 0;
@@ -493,7 +495,7 @@ __global__ void __launch_bounds__(STEP_THREADS, MINB) step_vec_kernel(StepArgs A
         const float4 cpv = ncp;
         const int32_t re = nre;
         const float vr = nvr;
-        if (r + STEP_THREADS / 32 < STEP_ROWS) prefetch(n + STEP_THREADS / 32);
+        if (r + STEP_THREADS / 32 < rows_pb) prefetch(n + STEP_THREADS / 32);
         if (active) {
             int32_t* pw = A.packed + n * A.ldp + k0;
             float cp[VEC] = {cpv.x, cpv.y, cpv.z, cpv.w};
@@ -688,7 +690,13 @@ static int step_impl(const concord_step_params* p, int32_t* packed, int64_t ldp,
     if (use_cp) vec = vec && (ldc % VEC == 0) && aligned(coh_pre, 16);
     cudaStream_t s = as_stream(stream);
     if (vec) {
-        dim3 grid((unsigned)((K + STEP_COLS - 1) / STEP_COLS), (unsigned)((N + STEP_ROWS - 1) / STEP_ROWS));
+        // 64 rows per block, fewer while the grid would cover under ~4 blocks per SM:
+        // a thread walks its rows one after another, so small layers need more blocks
+        const int64_t cblocks = (K + STEP_COLS - 1) / STEP_COLS;
+        int rpb = STEP_ROWS;
+        while (rpb > 8 && cblocks * ((N + rpb - 1) / rpb) < 148 * 4) rpb /= 2;
+        A.rows_per_block = rpb;
+        dim3 grid((unsigned)cblocks, (unsigned)((N + rpb - 1) / rpb));
         if (grid.y > 65535) return fail(CONCORD_ETOOBIG, "concord_step: too many rows for one launch");
         // resident blocks per SM the register budget targets (default 2; CONCORD_STEP_MINB=3)
         static const int minb = [] {
