@@ -11,11 +11,9 @@
 //
 // Each GEMM is a CUTLASS 4 sm100 warp-specialised kernel instantiated here:
 // TMA producer warp -> shared-memory ring -> one thread issuing
-// tcgen05.mma into TMEM -> epilogue warps reading TMEM with tcgen05.ld and
-// storing through TMA.  Default: cta_group::2, one 256x256x64 tile per CTA
-// pair on a 2x1x1 cluster (the pair shares the B tile); fallback: cta_group::1
-// 128x256x64 tiles, cluster 1x1x1.  With one CTA pair per cluster, every TMA
-// load has a single destination (the same kernels run in multi-GPU jobs).
+// tcgen05.mma (cta_group::1, 128x256x64 tiles) into TMEM -> epilogue warps
+// reading TMEM with tcgen05.ld and storing through TMA.  Cluster shape 1x1x1:
+// every TMA load is a single-CTA load (the same kernels run in multi-GPU jobs).
 #include <cuda_runtime.h>
 
 #include "cute/tensor.hpp"
@@ -62,40 +60,6 @@ CONCORD_DEFINE_GEMM(GemmFwd, cutlass::layout::RowMajor, cutlass::layout::ColumnM
 CONCORD_DEFINE_GEMM(GemmDx, cutlass::layout::RowMajor, cutlass::layout::RowMajor)
 CONCORD_DEFINE_GEMM(GemmDw, cutlass::layout::ColumnMajor, cutlass::layout::RowMajor)
 
-// 2-SM variants: one 256x256x64 MMA tile per CTA pair (cta_group::2), cluster
-// 2x1x1 -- the pair shares the B tile; with one CTA pair per cluster every TMA
-// load stays a plain (single-destination) 2-SM load
-using TileMNK2 = Shape<_256, _256, _64>;
-using Cluster2 = Shape<_2, _1, _1>;
-using Epi2 = typename cutlass::epilogue::collective::CollectiveBuilder<
-    cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, TileMNK2, Cluster2,
-    cutlass::epilogue::collective::EpilogueTileAuto, Acc, Acc, BF16, LayoutC, kAlign, BF16, LayoutC, kAlign,
-    cutlass::epilogue::TmaWarpSpecialized2Sm>::CollectiveOp;
-constexpr int kEpiSmem2 = static_cast<int>(sizeof(typename Epi2::SharedStorage));
-
-#define CONCORD_DEFINE_GEMM2(NAME, LA, LB)                                                                   \
-    using NAME##Main = typename cutlass::gemm::collective::CollectiveBuilder<                               \
-        cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, BF16, LA, kAlign, BF16, LB, kAlign, Acc,    \
-        TileMNK2, Cluster2, cutlass::gemm::collective::StageCountAutoCarveout<kEpiSmem2>,                   \
-        cutlass::gemm::KernelTmaWarpSpecialized2SmSm100>::CollectiveOp;                                    \
-    using NAME##Kernel = cutlass::gemm::kernel::GemmUniversal<Shape<int, int, int, int>, NAME##Main, Epi2, void>; \
-    using NAME = cutlass::gemm::device::GemmUniversalAdapter<NAME##Kernel>;
-
-CONCORD_DEFINE_GEMM2(GemmFwd2, cutlass::layout::RowMajor, cutlass::layout::ColumnMajor)
-CONCORD_DEFINE_GEMM2(GemmDx2, cutlass::layout::RowMajor, cutlass::layout::RowMajor)
-CONCORD_DEFINE_GEMM2(GemmDw2, cutlass::layout::ColumnMajor, cutlass::layout::RowMajor)
-
-// 2-SM kernels by default (measured 1458-1544 TFLOP/s against 1206-1337 for
-// the 1-SM ones at C2's largest shape); CONCORD_GEMM_2SM=0 selects the 1-SM
-// family, which also serves any shape the 2-SM kernel refuses
-static bool use_2sm() {
-    static const int v = [] {
-        const char* e = getenv("CONCORD_GEMM_2SM");
-        return e ? atoi(e) : 1;
-    }();
-    return v != 0;
-}
-
 // D[m,n] = sum_k A[m,k] B[k,n]; strides from the problem's layouts.
 template <class Gemm>
 int run_gemm(const void* A, const void* B, void* D, int M, int N, int K, void* workspace, size_t ws_bytes,
@@ -141,11 +105,6 @@ extern "C" int concord_gemm_fwd(const uint16_t* x, const uint16_t* w, uint16_t* 
                                 void* workspace, size_t workspace_bytes, void* stream) {
     if (bad(x) || bad(w) || bad(y)) return concord::fail(CONCORD_EALIGN, "concord_gemm_fwd: null or unaligned pointer");
     if (M <= 0 || N <= 0 || K <= 0) return concord::fail(CONCORD_ESHAPE, "concord_gemm_fwd: bad shape");
-    if (use_2sm()) {
-        const int rc = run_gemm<GemmFwd2>(x, w, y, (int)M, (int)N, (int)K, workspace, workspace_bytes,
-                                  reinterpret_cast<cudaStream_t>(stream), false, nullptr, "concord_gemm_fwd");
-        if (rc != CONCORD_ESHAPE) return rc;
-    }
     return run_gemm<GemmFwd>(x, w, y, (int)M, (int)N, (int)K, workspace, workspace_bytes,
                              reinterpret_cast<cudaStream_t>(stream), false, nullptr, "concord_gemm_fwd");
 }
@@ -155,11 +114,6 @@ extern "C" int concord_gemm_dx(const uint16_t* dy, const uint16_t* w, uint16_t* 
                                void* workspace, size_t workspace_bytes, void* stream) {
     if (bad(dy) || bad(w) || bad(dx)) return concord::fail(CONCORD_EALIGN, "concord_gemm_dx: null or unaligned pointer");
     if (M <= 0 || N <= 0 || K <= 0) return concord::fail(CONCORD_ESHAPE, "concord_gemm_dx: bad shape");
-    if (use_2sm()) {
-        const int rc = run_gemm<GemmDx2>(dy, w, dx, (int)M, (int)K, (int)N, workspace, workspace_bytes,
-                                 reinterpret_cast<cudaStream_t>(stream), false, nullptr, "concord_gemm_dx");
-        if (rc != CONCORD_ESHAPE) return rc;
-    }
     return run_gemm<GemmDx>(dy, w, dx, (int)M, (int)K, (int)N, workspace, workspace_bytes,
                             reinterpret_cast<cudaStream_t>(stream), false, nullptr, "concord_gemm_dx");
 }
@@ -169,22 +123,14 @@ extern "C" int concord_gemm_dw(const uint16_t* dy, const uint16_t* x, uint16_t* 
                                void* workspace, size_t workspace_bytes, void* stream) {
     if (bad(dy) || bad(x) || bad(dw)) return concord::fail(CONCORD_EALIGN, "concord_gemm_dw: null or unaligned pointer");
     if (M <= 0 || N <= 0 || K <= 0) return concord::fail(CONCORD_ESHAPE, "concord_gemm_dw: bad shape");
-    if (use_2sm()) {
-        const int rc = run_gemm<GemmDw2>(dy, x, dw, (int)N, (int)K, (int)M, workspace, workspace_bytes,
-                                 reinterpret_cast<cudaStream_t>(stream), false, nullptr, "concord_gemm_dw");
-        if (rc != CONCORD_ESHAPE) return rc;
-    }
     return run_gemm<GemmDw>(dy, x, dw, (int)N, (int)K, (int)M, workspace, workspace_bytes,
                             reinterpret_cast<cudaStream_t>(stream), false, nullptr, "concord_gemm_dw");
 }
 
 extern "C" size_t concord_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
-    size_t a = 0, b = 0, c = 0, a2 = 0, b2 = 0, c2 = 0;
+    size_t a = 0, b = 0, c = 0;
     run_gemm<GemmFwd>(nullptr, nullptr, nullptr, (int)M, (int)N, (int)K, nullptr, 0, nullptr, true, &a, "");
     run_gemm<GemmDx>(nullptr, nullptr, nullptr, (int)M, (int)K, (int)N, nullptr, 0, nullptr, true, &b, "");
     run_gemm<GemmDw>(nullptr, nullptr, nullptr, (int)N, (int)K, (int)M, nullptr, 0, nullptr, true, &c, "");
-    run_gemm<GemmFwd2>(nullptr, nullptr, nullptr, (int)M, (int)N, (int)K, nullptr, 0, nullptr, true, &a2, "");
-    run_gemm<GemmDx2>(nullptr, nullptr, nullptr, (int)M, (int)K, (int)N, nullptr, 0, nullptr, true, &b2, "");
-    run_gemm<GemmDw2>(nullptr, nullptr, nullptr, (int)N, (int)K, (int)M, nullptr, 0, nullptr, true, &c2, "");
-    return std::max(std::max(a, std::max(b, c)), std::max(a2, std::max(b2, c2)));
+    return std::max(a, std::max(b, c));
 }
