@@ -221,15 +221,22 @@ __global__ void __launch_bounds__(VH_THREADS) vhat_fold_kernel(VhatArgs A, int n
     if ((int)blockIdx.x < ncb) {
         const int64_t col = (int64_t)blockIdx.x * VH_THREADS + threadIdx.x;
         if (col < A.K) {
-            // fixed order b = 0, 1, ..., nrb-1; the loads of 16 partials go out together
+            // fixed order b = 0, 1, ..., nrb-1; the loads of 32 partials go out together
             float t = __ldcg(A.cp + col);
             int b = 1;
-            for (; b + 16 <= A.nrb; b += 16) {
-                float v[16];
+            for (; b + 32 <= A.nrb; b += 32) {
+                float v[32];
 #pragma unroll
-                for (int u = 0; u < 16; ++u) v[u] = __ldcg(A.cp + (int64_t)(b + u) * A.K + col);
+                for (int u = 0; u < 32; ++u) v[u] = __ldcg(A.cp + (int64_t)(b + u) * A.K + col);
 #pragma unroll
-                for (int u = 0; u < 16; ++u) t = t + v[u];
+                for (int u = 0; u < 32; ++u) t = t + v[u];
+            }
+            for (; b + 8 <= A.nrb; b += 8) {
+                float v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) v[u] = __ldcg(A.cp + (int64_t)(b + u) * A.K + col);
+#pragma unroll
+                for (int u = 0; u < 8; ++u) t = t + v[u];
             }
             for (; b < A.nrb; ++b) t = t + __ldcg(A.cp + (int64_t)b * A.K + col);
             if (A.col_sum_out) A.col_sum_out[col] = t;
@@ -252,9 +259,16 @@ __global__ void __launch_bounds__(VH_THREADS) vhat_fold_kernel(VhatArgs A, int n
     }
     __syncthreads();
     if (!last) return;
-    // fixed order n = t, t+256, t+512, ...; the loads of 8 go out together
+    // fixed order n = t, t+256, t+512, ...; the loads of 32 (then 8) go out together
     float acc = 0.0f;
     int64_t m = threadIdx.x;
+    for (; m + 31 * VH_THREADS < A.N; m += 32 * VH_THREADS) {
+        float v[32];
+#pragma unroll
+        for (int u = 0; u < 32; ++u) v[u] = __ldcg(A.v_row + m + u * VH_THREADS);
+#pragma unroll
+        for (int u = 0; u < 32; ++u) acc = acc + v[u];
+    }
     for (; m + 7 * VH_THREADS < A.N; m += 8 * VH_THREADS) {
         float v[8];
 #pragma unroll
