@@ -341,7 +341,6 @@ def cpu_step_sample(oracle, packed, rexp, cexp, grad, row0, v_row, v_col, svi, c
 
 def cpu_baseline(rows=2048, threads=1, reps=1):
     """Time the CPU restatement (oracle port) on `rows` x K of the workload."""
-    import ctypes  # noqa: F401
     oracle, packed, rexp, cexp, grad = oracle_sample(rows, K)
     chunks = np.array_split(np.arange(rows), threads)
     state = []

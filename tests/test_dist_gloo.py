@@ -13,7 +13,6 @@ import socket
 from types import SimpleNamespace
 
 import numpy as np
-import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
