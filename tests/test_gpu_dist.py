@@ -1,4 +1,4 @@
-"""Row-sharded data-parallel step on 2 (and 4) GPUs (skipped with fewer GPUs).
+"""Row-sharded data-parallel step on 2, 4 and 8 GPUs (skipped with fewer GPUs).
 
 Every rank must end with identical packed words, exponents, v-hat state and
 forward weight, equal bit for bit to a one-GPU emulation of the same sharded
@@ -117,7 +117,7 @@ def _free_port():
     return p
 
 
-@pytest.mark.parametrize("world,transport", [(2, "collective"), (2, "peer"), (4, "peer")])
+@pytest.mark.parametrize("world,transport", [(2, "collective"), (2, "peer"), (4, "peer"), (8, "peer")])
 @pytest.mark.parametrize("N", [300, 301])   # even split (in-place collectives) and padded
 def test_row_sharded_step(tmp_path, N, world, transport):
     if torch.cuda.device_count() < world:
