@@ -85,3 +85,68 @@ def grad_weight(grad_y_flat, x_flat):
     if g.dtype != torch.bfloat16:
         g = g.to(torch.bfloat16)
     return g.contiguous()
+
+
+# ---- convolutions as GEMMs over the unfolded input (im2col) ----
+#
+# The packed conv weight is the [O, I*kh*kw] matrix (the reference views its
+# Conv2d state that way, packed_b.py:2024-2065); unfold orders a column's
+# I*kh*kw entries (channel, kernel row, kernel column), the order of that
+# matrix's columns, so with cols = unfold(x) as [B*L, I*kh*kw] (L output
+# positions per image) the convolution is forward(cols, W), its input
+# gradient is fold(grad_input(dY, W)) and its weight gradient is
+# grad_weight(dY, cols): the three GEMMs of the Linear layer.
+
+def _pair(v):
+    return (v, v) if isinstance(v, int) else tuple(v)
+
+
+def _conv_out(H, W, kh, kw, stride, padding):
+    st, pd = _pair(stride), _pair(padding)
+    return (H + 2 * pd[0] - kh) // st[0] + 1, (W + 2 * pd[1] - kw) // st[1] + 1
+
+
+def _conv_cols(x, kh, kw, stride, padding):
+    """unfold(x) as a contiguous [B*L, C*kh*kw] matrix, plus (Ho, Wo)."""
+    B, C, H, W = x.shape
+    Ho, Wo = _conv_out(H, W, kh, kw, stride, padding)
+    cols = F.unfold(x, (kh, kw), padding=_pair(padding), stride=_pair(stride))   # [B, C*kh*kw, L]
+    return cols.transpose(1, 2).reshape(B * Ho * Wo, C * kh * kw), Ho, Wo
+
+
+def conv_usable(x, weight_2d, kh, kw, stride, padding):
+    """True when the GEMM form of this convolution runs this package's kernels."""
+    if x.dim() != 4 or not _usable(x, weight_2d):
+        return False
+    B, C, H, W = x.shape
+    Ho, Wo = _conv_out(H, W, kh, kw, stride, padding)
+    O, IK = weight_2d.shape
+    return Ho > 0 and Wo > 0 and _ok(B * Ho * Wo, O, IK)
+
+
+def conv2d_forward(x, weight_2d, bias, kh, kw, stride, padding):
+    """y = conv2d(x, W) (NCHW, bf16) through the forward GEMM."""
+    B = x.shape[0]
+    O = weight_2d.shape[0]
+    cols, Ho, Wo = _conv_cols(x, kh, kw, stride, padding)
+    y = forward(cols, weight_2d)                                   # [B*L, O]
+    y = y.view(B, Ho, Wo, O).permute(0, 3, 1, 2).contiguous()
+    if bias is not None:
+        y.add_(bias.view(1, O, 1, 1))
+    return y
+
+
+def conv2d_backward(x, weight_2d, grad_y, kh, kw, stride, padding):
+    """(dX, dW) of conv2d(x, W) for the NCHW gradient grad_y.  dW is the bf16
+    [O, I*kh*kw] matrix the packed step consumes (fp32 accumulation, one
+    rounding); dX sums the kh*kw bf16 column gradients of each pixel in fp32
+    (fold) and rounds again."""
+    B, C, H, W = x.shape
+    O = weight_2d.shape[0]
+    cols, Ho, Wo = _conv_cols(x, kh, kw, stride, padding)
+    gy = grad_y.permute(0, 2, 3, 1).reshape(B * Ho * Wo, O).contiguous()
+    dW = grad_weight(gy, cols)
+    dcols = grad_input(gy, weight_2d)                               # [B*L, C*kh*kw]
+    dcols = dcols.view(B, Ho * Wo, C * kh * kw).transpose(1, 2)
+    dx = F.fold(dcols, (H, W), (kh, kw), padding=_pair(padding), stride=_pair(stride))
+    return dx, dW

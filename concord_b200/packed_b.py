@@ -858,9 +858,11 @@ class ConcordLinearPackedB(nn.Module):
 class FusedConcordConv2dPackedB(torch.autograd.Function):
     """Conv2d whose backward is the packed step (packed_b.py:1863-2021).
 
-    The convolutions run in cuDNN (library); the weight is the packed
-    [O, I*kh*kw] matrix and the optimizer half is the same two launches as
-    the Linear layer.
+    The weight is the packed [O, I*kh*kw] matrix.  When the GEMM extents
+    (B*Ho*Wo, O, I*kh*kw) are multiples of 8 the convolutions run as this
+    package's GEMMs over the unfolded input (gemm.conv2d_forward /
+    conv2d_backward); other shapes use cuDNN, as the reference does for every
+    shape.  The optimizer half is the same launches as the Linear layer.
     """
 
     @staticmethod
@@ -875,8 +877,12 @@ class FusedConcordConv2dPackedB(torch.autograd.Function):
         x_bf16 = x_bf16.contiguous()
         bias_bf16 = (bias.to(torch.bfloat16)
                      if bias is not None and bias.dtype != torch.bfloat16 else bias)
-        y = torch.nn.functional.conv2d(x_bf16, weight_4d, bias=bias_bf16, stride=stride,
-                                       padding=padding)
+        ctx.gemm = _gemm.conv_usable(x_bf16, weight_buf, kh, kw, stride, padding)
+        if ctx.gemm:
+            y = _gemm.conv2d_forward(x_bf16, weight_buf, bias_bf16, kh, kw, stride, padding)
+        else:
+            y = torch.nn.functional.conv2d(x_bf16, weight_4d, bias=bias_bf16, stride=stride,
+                                           padding=padding)
         ctx.save_for_backward(x_bf16, weight_4d)
         vals = (packed_w, row_exp, col_exp, lr, alpha, beta1, mantissa_bias, optimizer_kind,
                 weight_decay, eps, step_cap, v_scale, precond_p, gf_consol, drift_cancel_C,
@@ -897,11 +903,15 @@ class FusedConcordConv2dPackedB(torch.autograd.Function):
         if grad_y.dtype != torch.bfloat16:
             grad_y = grad_y.to(torch.bfloat16)
         grad_y = grad_y.contiguous()
-        grad_x = torch.nn.grad.conv2d_input(x_bf16.shape, weight_4d, grad_y, stride=stride,
-                                            padding=padding)
-        grad_W = torch.nn.grad.conv2d_weight(x_bf16, (out_c, in_c, kh, kw), grad_y, stride=stride,
-                                             padding=padding)
-        grad_W = grad_W.reshape(out_c, -1).to(torch.bfloat16).contiguous()
+        if ctx.gemm:
+            grad_x, grad_W = _gemm.conv2d_backward(x_bf16, weight_4d.view(out_c, -1), grad_y, kh, kw,
+                                                   stride, padding)
+        else:
+            grad_x = torch.nn.grad.conv2d_input(x_bf16.shape, weight_4d, grad_y, stride=stride,
+                                                padding=padding)
+            grad_W = torch.nn.grad.conv2d_weight(x_bf16, (out_c, in_c, kh, kw), grad_y,
+                                                 stride=stride, padding=padding)
+            grad_W = grad_W.reshape(out_c, -1).to(torch.bfloat16).contiguous()
         _packed_backward_step(ctx, grad_W)
         grad_bias = grad_y.sum(dim=(0, 2, 3)) if ctx.has_bias else None
         return (grad_x, None, None, None, grad_bias) + (None,) * 35
