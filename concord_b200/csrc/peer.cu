@@ -50,19 +50,26 @@ __global__ void __launch_bounds__(PEER_THREADS) peer_push_kernel(const uint4* gr
         // this rank's own rows stay where they are: chunks [own0, own1) are skipped
         const I own0 = (I)min((int64_t)total, (int64_t)s.rank * S64 * kc64);
         const I own1 = (I)min((int64_t)total, ((int64_t)s.rank + 1) * S64 * kc64);
+        // the other chunks in the order own1, ..., total-1, 0, ..., own0-1: at any
+        // moment rank r writes mostly to rank r+1's shard, rank r+1 to r+2's, and
+        // so on, so the ranks' stores spread over every receiver instead of all
+        // ranks writing the same receiver's shard at once
+        const I work = total - (own1 - own0);
         const I span = (I)gridDim.x * PEER_THREADS;
-        for (I c0 = (I)blockIdx.x * PEER_THREADS + threadIdx.x; c0 < total; c0 += span * PUSH_UNROLL) {
+        for (I i0 = (I)blockIdx.x * PEER_THREADS + threadIdx.x; i0 < work; i0 += span * PUSH_UNROLL) {
             uint4 v[PUSH_UNROLL];
-            bool go[PUSH_UNROLL];
+            I cs[PUSH_UNROLL];
 #pragma unroll
             for (int u = 0; u < PUSH_UNROLL; ++u) {
-                const I c = c0 + (I)u * span;
-                go[u] = c < total && (c < own0 || c >= own1);
-                if (go[u]) v[u] = __ldcs(grad + c);
+                const I i = i0 + (I)u * span;
+                I c = own1 + i;
+                if (c >= total) c -= total;
+                cs[u] = c;
+                if (i < work) v[u] = __ldcs(grad + c);
             }
 #pragma unroll
             for (int u = 0; u < PUSH_UNROLL; ++u)
-                if (go[u]) push_chunk<I>(grad, recv, c0 + (I)u * span, kc, S, s.rank, v[u]);
+                if (i0 + (I)u * span < work) push_chunk<I>(grad, recv, cs[u], kc, S, s.rank, v[u]);
         }
     }
     __syncthreads();

@@ -571,7 +571,9 @@ __global__ void __launch_bounds__(STEP_THREADS, MINB) step_vec_kernel(StepArgs A
             const bool pair = peer16 && (k0 + VEC) < A.K;
             if (active && (!peer16 || !(lane & 1))) {
                 const int64_t off = (A.row0 + n) * A.ldw + k0;
-                for (int q = 0; q < A.npeers; ++q) {
+                // each row starts at another peer, spreading the stores over the links
+                int q = (int)(n % A.npeers);
+                for (int t = 0; t < A.npeers; ++t, q = (q + 1 == A.npeers) ? 0 : q + 1) {
                     uint16_t* dst = reinterpret_cast<uint16_t*>(A.wpeers[q]) + off;
                     if (pair) __stcs(reinterpret_cast<uint4*>(dst), make_uint4(wb.x, wb.y, hx, hy));
                     else __stcs(reinterpret_cast<uint2*>(dst), wb);
