@@ -186,6 +186,10 @@ _SIGS = [
     ("concord_gemm_fwd", ctypes.c_int, [_P, _P, _P, _I64, _I64, _I64, _P, ctypes.c_size_t, _P]),
     ("concord_gemm_dx", ctypes.c_int, [_P, _P, _P, _I64, _I64, _I64, _P, ctypes.c_size_t, _P]),
     ("concord_gemm_dw", ctypes.c_int, [_P, _P, _P, _I64, _I64, _I64, _P, ctypes.c_size_t, _P]),
+    ("concord_im2col", ctypes.c_int,
+     [_P, _I64, _I64, _I64, _I64, _I32, _I32, _I32, _I32, _I32, _I32, _P, _P]),
+    ("concord_col2im", ctypes.c_int,
+     [_P, _I64, _I64, _I64, _I64, _I32, _I32, _I32, _I32, _I32, _I32, _P, _P]),
 ]
 
 EXPORTED = [s[0] for s in _SIGS]

@@ -87,31 +87,44 @@ def grad_weight(grad_y_flat, x_flat):
     return g.contiguous()
 
 
-# ---- convolutions as GEMMs over the unfolded input (im2col) ----
+# ---- convolutions as GEMMs over a column matrix (im2col) ----
 #
 # The packed conv weight is the [O, I*kh*kw] matrix (the reference views its
-# Conv2d state that way, packed_b.py:2024-2065); unfold orders a column's
-# I*kh*kw entries (channel, kernel row, kernel column), the order of that
-# matrix's columns, so with cols = unfold(x) as [B*L, I*kh*kw] (L output
-# positions per image) the convolution is forward(cols, W), its input
-# gradient is fold(grad_input(dY, W)) and its weight gradient is
-# grad_weight(dY, cols): the three GEMMs of the Linear layer.
+# Conv2d state that way, packed_b.py:2024-2065).  concord_im2col writes
+# cols [B*Ho*Wo, I*kh*kw] with columns in (channel, kernel row, kernel
+# column) order, the order of that matrix's columns, so
+#   y^T [O, B*Ho*Wo]      = forward GEMM of (W, cols)      (NCHW at B == 1)
+#   dW  [O, I*kh*kw]      = dW GEMM of (dY as [B*Ho*Wo, O], cols)
+#   dcols^T [I*kh*kw, M]  = forward GEMM of (W^T, dY as [M, O]), then
+#                           concord_col2im sums each pixel's kh*kw entries.
 
 def _pair(v):
-    return (v, v) if isinstance(v, int) else tuple(v)
+    return (int(v), int(v)) if isinstance(v, int) else tuple(int(a) for a in v)
 
 
 def _conv_out(H, W, kh, kw, stride, padding):
     st, pd = _pair(stride), _pair(padding)
+    if H + 2 * pd[0] < kh or W + 2 * pd[1] < kw:
+        return 0, 0
     return (H + 2 * pd[0] - kh) // st[0] + 1, (W + 2 * pd[1] - kw) // st[1] + 1
 
 
+def _geom(x, kh, kw, stride, padding):
+    B, C, H, W = x.shape
+    st, pd = _pair(stride), _pair(padding)
+    return (B, C, H, W, kh, kw, st[0], st[1], pd[0], pd[1])
+
+
 def _conv_cols(x, kh, kw, stride, padding):
-    """unfold(x) as a contiguous [B*L, C*kh*kw] matrix, plus (Ho, Wo)."""
+    """The column matrix [B*Ho*Wo, C*kh*kw] of the bf16 NCHW input, plus (Ho, Wo)."""
     B, C, H, W = x.shape
     Ho, Wo = _conv_out(H, W, kh, kw, stride, padding)
-    cols = F.unfold(x, (kh, kw), padding=_pair(padding), stride=_pair(stride))   # [B, C*kh*kw, L]
-    return cols.transpose(1, 2).reshape(B * Ho * Wo, C * kh * kw), Ho, Wo
+    x = x.contiguous()
+    cols = torch.empty(B * Ho * Wo, C * kh * kw, dtype=torch.bfloat16, device=x.device)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)
+    _abi.check(_abi.load().concord_im2col(_ptr(x), *_geom(x, kh, kw, stride, padding), _ptr(cols), stream),
+               "concord_im2col")
+    return cols, Ho, Wo
 
 
 def conv_usable(x, weight_2d, kh, kw, stride, padding):
@@ -121,16 +134,19 @@ def conv_usable(x, weight_2d, kh, kw, stride, padding):
     B, C, H, W = x.shape
     Ho, Wo = _conv_out(H, W, kh, kw, stride, padding)
     O, IK = weight_2d.shape
-    return Ho > 0 and Wo > 0 and _ok(B * Ho * Wo, O, IK)
+    return Ho > 0 and Wo > 0 and IK == C * kh * kw and _ok(B * Ho * Wo, O, IK)
 
 
 def conv2d_forward(x, weight_2d, bias, kh, kw, stride, padding):
-    """y = conv2d(x, W) (NCHW, bf16) through the forward GEMM."""
+    """y = conv2d(x, W) (NCHW, bf16): the forward GEMM of (W, cols)."""
     B = x.shape[0]
     O = weight_2d.shape[0]
     cols, Ho, Wo = _conv_cols(x, kh, kw, stride, padding)
-    y = forward(cols, weight_2d)                                   # [B*L, O]
-    y = y.view(B, Ho, Wo, O).permute(0, 3, 1, 2).contiguous()
+    yt = forward(weight_2d, cols)                                  # [O, B*Ho*Wo]
+    if B == 1:
+        y = yt.view(1, O, Ho, Wo)
+    else:
+        y = yt.view(O, B, Ho, Wo).transpose(0, 1).contiguous()
     if bias is not None:
         y.add_(bias.view(1, O, 1, 1))
     return y
@@ -139,14 +155,17 @@ def conv2d_forward(x, weight_2d, bias, kh, kw, stride, padding):
 def conv2d_backward(x, weight_2d, grad_y, kh, kw, stride, padding):
     """(dX, dW) of conv2d(x, W) for the NCHW gradient grad_y.  dW is the bf16
     [O, I*kh*kw] matrix the packed step consumes (fp32 accumulation, one
-    rounding); dX sums the kh*kw bf16 column gradients of each pixel in fp32
-    (fold) and rounds again."""
+    rounding); dX sums each pixel's kh*kw bf16 column gradients in fp32
+    (concord_col2im) and rounds again."""
     B, C, H, W = x.shape
     O = weight_2d.shape[0]
     cols, Ho, Wo = _conv_cols(x, kh, kw, stride, padding)
     gy = grad_y.permute(0, 2, 3, 1).reshape(B * Ho * Wo, O).contiguous()
     dW = grad_weight(gy, cols)
-    dcols = grad_input(gy, weight_2d)                               # [B*L, C*kh*kw]
-    dcols = dcols.view(B, Ho * Wo, C * kh * kw).transpose(1, 2)
-    dx = F.fold(dcols, (H, W), (kh, kw), padding=_pair(padding), stride=_pair(stride))
+    del cols
+    dcols_t = forward(weight_2d.t().contiguous(), gy)               # [C*kh*kw, B*Ho*Wo]
+    dx = torch.empty(B, C, H, W, dtype=torch.bfloat16, device=x.device)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)
+    _abi.check(_abi.load().concord_col2im(_ptr(dcols_t), *_geom(x, kh, kw, stride, padding), _ptr(dx),
+                                          stream), "concord_col2im")
     return dx, dW

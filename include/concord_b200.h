@@ -41,6 +41,10 @@
  *                            (packed_b.py:2081-2106)
  *   concord_gemm_fwd/dx/dw <- F.linear / grad_y @ W / grad_y^T @ x
  *                            (packed_b.py:1219, 1263, 1271-1277)
+ *   concord_im2col / concord_col2im <- the data movement inside torch's
+ *                            conv2d / conv2d_input used by the conv layer
+ *                            (packed_b.py:2024-2065); with them the conv
+ *                            runs on concord_gemm_*
  * The peer-memory entry points (concord_peer_*, concord_ipc_*,
  * concord_step_sharded) have no counterpart: the reference is single-GPU.
  */
@@ -418,6 +422,22 @@ int concord_gemm_dx(const uint16_t* dy, const uint16_t* w, uint16_t* dx, int64_t
                     void* workspace, size_t workspace_bytes, void* stream);
 int concord_gemm_dw(const uint16_t* dy, const uint16_t* x, uint16_t* dw, int64_t M, int64_t N, int64_t K,
                     void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Convolution as GEMMs (bf16, NCHW input x [B, C, H, W], kernel kh x kw,
+ * stride sh/sw, zero padding ph/pw; Ho = (H + 2ph - kh)/sh + 1, likewise Wo).
+ * im2col: cols [B*Ho*Wo, C*kh*kw] row-major, column c*kh*kw + i*kw + j
+ * (the order of the packed [O, C*kh*kw] weight); C*kh*kw % 8 == 0, cols
+ * 16-byte aligned.  col2im: dx [B, C, H, W] from the transposed column
+ * gradient dcols_t [C*kh*kw, B*Ho*Wo], each pixel summed in fp32 over
+ * (i, j) in order and rounded once to bf16.
+ */
+int concord_im2col(const uint16_t* x, int64_t B, int64_t C, int64_t H, int64_t W,
+                   int32_t kh, int32_t kw, int32_t sh, int32_t sw, int32_t ph, int32_t pw,
+                   uint16_t* cols, void* stream);
+int concord_col2im(const uint16_t* dcols_t, int64_t B, int64_t C, int64_t H, int64_t W,
+                   int32_t kh, int32_t kw, int32_t sh, int32_t sw, int32_t ph, int32_t pw,
+                   uint16_t* dx, void* stream);
 
 #ifdef __cplusplus
 }

@@ -1,10 +1,12 @@
-"""Conv2d through this package's GEMMs over the unfolded input.
+"""Conv2d through this package's GEMMs over a column matrix (im2col).
 
 ConcordConv2dPackedB runs its three convolutions as the Linear layer's GEMMs
-on unfold(x) when the GEMM extents are multiples of 8.  Checked: the
-forward, dX and dW against fp32 convolutions of the same bf16 values (bf16
-output tolerance written per check), and the whole layer step against a
-Linear layer with the same packed state fed the unfolded input, which must
+on the column matrix when the GEMM extents are multiples of 8.  Checked:
+concord_im2col against torch's unfold (bit for bit: a copy),
+concord_col2im against a float64 fold of the same bf16 column gradient,
+the forward, dX and dW against fp32 convolutions of the same bf16 values
+(bf16 output tolerance written per check), and the whole layer step against
+a Linear layer with the same packed state fed the column matrix, which must
 give the same words bit for bit (the same dW reaches the same step).
 """
 import pytest
@@ -24,6 +26,29 @@ CASES = [  # B, C, H, W, O, k, stride, padding
 
 def _bf(t):
     return t.to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_im2col_col2im_match_unfold_fold(case):
+    from concord_b200 import gemm
+    B, C, H, W, O, k, st, pd = case
+    g = torch.Generator(device="cpu").manual_seed(7 + sum(case))
+    x = _bf(torch.randn(B, C, H, W, generator=g)).to(DEV)
+    cols, Ho, Wo = gemm._conv_cols(x, k, k, st, pd)
+    ref = F.unfold(x, (k, k), padding=pd, stride=st).transpose(1, 2).reshape(B * Ho * Wo, -1)
+    assert torch.equal(cols, ref)
+    dct = _bf(torch.randn(C * k * k, B * Ho * Wo, generator=g)).to(DEV)
+    dx = torch.empty_like(x)
+    import ctypes
+    s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    from concord_b200 import _abi
+    _abi.check(_abi.load().concord_col2im(ctypes.c_void_p(dct.data_ptr()), *gemm._geom(x, k, k, st, pd),
+                                          ctypes.c_void_p(dx.data_ptr()), s), "col2im")
+    cols64 = dct.double().view(C * k * k, B, Ho * Wo).transpose(0, 1)
+    dx64 = F.fold(cols64, (H, W), (k, k), padding=pd, stride=st)
+    # fp32 sum of at most k*k terms, then one bf16 rounding
+    err = (dx.double() - dx64).abs()
+    assert (err <= 2.0 ** -8 * dx64.abs() + 1e-5 * dx64.abs().max()).all()
 
 
 @pytest.mark.parametrize("case", CASES)
@@ -77,7 +102,9 @@ def test_conv_layer_step_equals_linear_on_unfolded_input():
         set_step_salt(DEV, 100 + t)
         yl = lin(cols)
         yl.backward(gy.permute(0, 2, 3, 1).reshape(B * Ho * Wo, O))
-        assert torch.equal(y.permute(0, 2, 3, 1).reshape(-1, O), yl)
+        # same products, GEMMs in the other orientation: within bf16 rounding
+        yc = y.permute(0, 2, 3, 1).reshape(-1, O).float()
+        assert (yc - yl.float()).abs().max().item() <= 2.0 ** -7 * yl.float().abs().max().item()
         assert torch.equal(conv.packed_w, lin.packed_w), t
         conv.rebalance()
         lin.rebalance()
