@@ -18,6 +18,7 @@ from .packed_b import (  # noqa: F401
     set_consolidate,
     set_sigmag_noise,
     set_sigmag_sigma,
+    set_conv_backend,
     reset_reb_stats,
     get_reb_stats,
     gate_coherence_from_fields,
@@ -42,6 +43,7 @@ __all__ = [
     "set_gate_gain",
     "reset_reb_stats",
     "get_reb_stats",
+    "set_conv_backend",
     "S_SLOW_FACTOR",
     "V_SLOW_FACTOR",
     "MANTISSA_BIAS",

@@ -57,7 +57,7 @@ _KNOBS = ("alpha", "beta1", "optimizer_kind", "weight_decay", "_eps_value", "_lr
           "track_adafactor_v", "adafactor_beta2", "gf_trust_delta_sq", "allow_tickdown", "wd_sv",
           "wd_sf", "mass_preserve_v", "apply_chase", "track_rebalance")
 _GLOBALS = ("_USE_FIXED_COH", "_GATE_GAIN", "_COH_WEIGHTED_V", "_RATIO_COH", "_RATIO_CHASE_FLOOR",
-            "_RATIO_LEAK_FLOOR", "_FLOOR_TENSORS_ON", "_SIGMAG_NOISE", "_SIGMAG_ISO", "_SIGMAG_SIGMA")
+            "_RATIO_LEAK_FLOOR", "_FLOOR_TENSORS_ON", "_SIGMAG_NOISE", "_SIGMAG_ISO", "_SIGMAG_SIGMA", "_CONV_BACKEND")
 
 
 def save_state(model):

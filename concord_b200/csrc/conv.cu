@@ -8,8 +8,8 @@
 // column matrix whose columns follow that view's order (channel, kernel row,
 // kernel column):
 //   im2col : cols[m, c*kh*kw + i*kw + j] = x[b, c, ho*sh - ph + i, wo*sw - pw + j]
-//            (zero outside the image), m = (b*Ho + ho)*Wo + wo; one pass, one
-//            16-byte store of 8 columns per thread.
+//            (zero outside the image), m = (b*Ho + ho)*Wo + wo; one pass,
+//            transposed through shared memory, 16-byte stores.
 //   col2im : dx[b, c, h, w] = sum over (i, j) of dcolsT[c*kh*kw + i*kw + j, m]
 //            for the m whose window covers (h, w) at (i, j); the column
 //            gradient arrives transposed ([C*kh*kw, B*Ho*Wo], the GEMM writes
@@ -24,63 +24,108 @@ struct ConvGeom {
     int32_t kh, kw, sh, sw, ph, pw;
 };
 
-__global__ void im2col_kernel(const uint16_t* __restrict__ x, uint16_t* __restrict__ cols, ConvGeom g) {
+// One block per tile of IM_TM output positions x IM_TC columns.  A table of
+// the tile's columns (input offset and kernel position) is built once per
+// block; the gather runs with neighbouring threads on neighbouring positions
+// (for stride 1, neighbouring input pixels) into a [column][position] tile,
+// and the store runs 16 bytes (8 columns of one position) per thread.
+constexpr int IM_TM = 64, IM_TC = 64, IM_THREADS = 256;
+
+__global__ void __launch_bounds__(IM_THREADS) im2col_kernel(const uint16_t* __restrict__ x,
+                                                            uint16_t* __restrict__ cols, ConvGeom g) {
+    __shared__ uint16_t tile[IM_TC][IM_TM + 2];
+    __shared__ int64_t coff[IM_TC];
+    __shared__ int32_t cki[IM_TC], ckj[IM_TC];
     const int32_t kk = g.kh * g.kw;
-    const int64_t ckk = g.C * kk;
-    const int64_t groups = ckk / 8;
-    const int64_t L = g.Ho * g.Wo;
-    const int64_t total = g.B * L * groups;
-    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
-         t += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t m = t / groups;
-        const int64_t col0 = (t - m * groups) * 8;
-        const int64_t b = m / L;
-        const int64_t p = m - b * L;
-        const int64_t ho = p / g.Wo, wo = p - ho * g.Wo;
-        const int64_t h0 = ho * g.sh - g.ph, w0 = wo * g.sw - g.pw;
-        int64_t c = col0 / kk;
-        int32_t r = (int32_t)(col0 - c * kk);
-        int32_t i = r / g.kw, j = r - i * g.kw;
-        uint32_t v[4];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            const int64_t h = h0 + i, w = w0 + j;
-            uint32_t val = 0;
-            if (h >= 0 && h < g.H && w >= 0 && w < g.W) val = x[((b * g.C + c) * g.H + h) * g.W + w];
-            if (e & 1) v[e >> 1] |= val << 16;
-            else v[e >> 1] = val;
-            if (++j == g.kw) { j = 0; if (++i == g.kh) { i = 0; ++c; } }
+    const int32_t ckk = (int32_t)g.C * kk;
+    const int32_t L = (int32_t)(g.Ho * g.Wo);
+    const int64_t M = g.B * L;
+    const int64_t m0 = (int64_t)blockIdx.x * IM_TM;
+    const int32_t c0 = (int32_t)blockIdx.y * IM_TC;
+    const int64_t plane = g.H * g.W;
+    if (threadIdx.x < IM_TC) {
+        const int32_t col = c0 + threadIdx.x;
+        int32_t i = -(1 << 29), j = 0;   // columns past the end never pass the bounds test
+        int64_t off = 0;
+        if (col < ckk) {
+            const int32_t c = col / kk, r = col - c * kk;
+            i = r / g.kw;
+            j = r - i * g.kw;
+            off = (int64_t)c * plane + (int64_t)i * g.W + j;
         }
-        reinterpret_cast<uint4*>(cols)[t] = make_uint4(v[0], v[1], v[2], v[3]);
+        coff[threadIdx.x] = off; cki[threadIdx.x] = i; ckj[threadIdx.x] = j;
+    }
+    __syncthreads();
+    {
+        const int32_t mi = threadIdx.x % IM_TM;
+        const int64_t m = m0 + mi;
+        const bool mok = m < M;
+        const int32_t b = mok ? (int32_t)(m / L) : 0;
+        const int32_t p = mok ? (int32_t)(m - (int64_t)b * L) : 0;
+        const int32_t ho = p / (int32_t)g.Wo, wo = p - ho * (int32_t)g.Wo;
+        const int32_t h0 = mok ? ho * g.sh - g.ph : -(1 << 29), w0 = wo * g.sw - g.pw;
+        const int64_t base = (int64_t)b * g.C * plane + (int64_t)h0 * g.W + w0;
+#pragma unroll 4
+        for (int32_t ci = threadIdx.x / IM_TM; ci < IM_TC; ci += IM_THREADS / IM_TM) {
+            const int32_t h = h0 + cki[ci], w = w0 + ckj[ci];
+            uint16_t v = 0;
+            if ((uint32_t)h < (uint32_t)g.H && (uint32_t)w < (uint32_t)g.W) v = x[base + coff[ci]];
+            tile[ci][mi] = v;
+        }
+    }
+    __syncthreads();
+    for (int q = threadIdx.x; q < IM_TM * (IM_TC / 8); q += IM_THREADS) {
+        const int32_t mi = q >> 3, ch = q & 7;
+        const int64_t m = m0 + mi;
+        const int32_t col = c0 + ch * 8;
+        if (m < M && col < ckk) {
+            uint32_t v[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                v[e] = (uint32_t)tile[ch * 8 + 2 * e][mi] | ((uint32_t)tile[ch * 8 + 2 * e + 1][mi] << 16);
+            *reinterpret_cast<uint4*>(cols + m * ckk + col) = make_uint4(v[0], v[1], v[2], v[3]);
+        }
     }
 }
 
+// blockIdx.x = (image, channel) plane; 32-bit index arithmetic inside it.
+// KH / KW: compile-time kernel size (0: read it from g)
+template <bool UNIT_STRIDE, int KH, int KW>
 __global__ void col2im_kernel(const uint16_t* __restrict__ dcolsT, uint16_t* __restrict__ dx, ConvGeom g) {
-    const int32_t kk = g.kh * g.kw;
+    const int32_t kh = KH ? KH : g.kh, kw = KW ? KW : g.kw;
+    const int32_t kk = kh * kw;
     const int64_t M = g.B * g.Ho * g.Wo;
-    const int64_t total = g.B * g.C * g.H * g.W;
-    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
-         t += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t w = t % g.W;
-        const int64_t h = (t / g.W) % g.H;
-        const int64_t c = (t / (g.W * g.H)) % g.C;
-        const int64_t b = t / (g.W * g.H * g.C);
+    const int32_t bc = blockIdx.x;
+    const int32_t b = bc / (int32_t)g.C, c = bc - b * (int32_t)g.C;
+    const int32_t H = (int32_t)g.H, W = (int32_t)g.W, Ho = (int32_t)g.Ho, Wo = (int32_t)g.Wo;
+    const int32_t plane = H * W;
+    const uint16_t* src = dcolsT + (int64_t)c * kk * M + (int64_t)b * Ho * Wo;
+    uint16_t* dst = dx + (int64_t)bc * plane;
+    for (int32_t t = blockIdx.y * blockDim.x + threadIdx.x; t < plane; t += gridDim.y * blockDim.x) {
+        const int32_t h = t / W, w = t - h * W;
         float acc = 0.0f;
-        for (int32_t i = 0; i < g.kh; ++i) {
-            const int64_t hs = h + g.ph - i;           // = ho * sh
-            if (hs < 0 || hs % g.sh) continue;
-            const int64_t ho = hs / g.sh;
-            if (ho >= g.Ho) continue;
-            for (int32_t j = 0; j < g.kw; ++j) {
-                const int64_t ws = w + g.pw - j;
-                if (ws < 0 || ws % g.sw) continue;
-                const int64_t wo = ws / g.sw;
-                if (wo >= g.Wo) continue;
-                const int64_t m = (b * g.Ho + ho) * g.Wo + wo;
-                acc = acc + bf16_to_f32(dcolsT[(c * kk + i * g.kw + j) * M + m]);
+#pragma unroll
+        for (int32_t i = 0; i < kh; ++i) {
+            int32_t ho = h + g.ph - i;                  // = ho * sh
+            if (ho < 0) continue;
+            if (!UNIT_STRIDE) {
+                if (ho % g.sh) continue;
+                ho /= g.sh;
+            }
+            if (ho >= Ho) continue;
+#pragma unroll
+            for (int32_t j = 0; j < kw; ++j) {
+                int32_t wo = w + g.pw - j;
+                if (wo < 0) continue;
+                if (!UNIT_STRIDE) {
+                    if (wo % g.sw) continue;
+                    wo /= g.sw;
+                }
+                if (wo >= Wo) continue;
+                acc = acc + bf16_to_f32(src[(int64_t)(i * kw + j) * M + ho * Wo + wo]);
             }
         }
-        dx[t] = f32_to_bf16(acc);
+        dst[t] = f32_to_bf16(acc);
     }
 }
 
@@ -96,12 +141,6 @@ static int make_geom(int64_t B, int64_t C, int64_t H, int64_t W, int32_t kh, int
     return CONCORD_OK;
 }
 
-static unsigned grid_for(int64_t total, int threads) {
-    int64_t blocks = (total + threads - 1) / threads;
-    const int64_t cap = 148LL * 16;   // grid-stride beyond 16 blocks per SM
-    return (unsigned)(blocks < 1 ? 1 : (blocks > cap ? cap : blocks));
-}
-
 }  // namespace concord
 
 using namespace concord;
@@ -114,10 +153,14 @@ extern "C" int concord_im2col(const uint16_t* x, int64_t B, int64_t C, int64_t H
     if (rc) return rc;
     if ((C * kh * kw) % 8 != 0) return fail(CONCORD_ESHAPE, "concord_im2col: C*kh*kw must be a multiple of 8");
     if (!aligned(cols, 16)) return fail(CONCORD_EALIGN, "concord_im2col: cols must be 16-byte aligned");
-    const int64_t total = B * g.Ho * g.Wo * (C * kh * kw / 8);
-    if (total == 0) return CONCORD_OK;
+    const int64_t M = B * g.Ho * g.Wo, ckk = C * kh * kw;
+    if (M == 0 || ckk == 0) return CONCORD_OK;
     if (!x || !cols) return fail(CONCORD_EINVAL, "concord_im2col: null pointer");
-    im2col_kernel<<<grid_for(total, 256), 256, 0, as_stream(stream)>>>(x, cols, g);
+    if (ckk > INT32_MAX || g.Ho * g.Wo > INT32_MAX || C * H * W > INT32_MAX || (M + IM_TM - 1) / IM_TM > INT32_MAX)
+        return fail(CONCORD_ESHAPE, "concord_im2col: extents above 32-bit tile indexing");
+    const dim3 grid((unsigned)((M + IM_TM - 1) / IM_TM), (unsigned)((ckk + IM_TC - 1) / IM_TC));
+    if (grid.y > 65535) return fail(CONCORD_ESHAPE, "concord_im2col: C*kh*kw too large");
+    im2col_kernel<<<grid, IM_THREADS, 0, as_stream(stream)>>>(x, cols, g);
     return check_launch("concord_im2col");
 }
 
@@ -130,6 +173,16 @@ extern "C" int concord_col2im(const uint16_t* dcols_t, int64_t B, int64_t C, int
     const int64_t total = B * C * H * W;
     if (total == 0) return CONCORD_OK;
     if (!dcols_t || !dx) return fail(CONCORD_EINVAL, "concord_col2im: null pointer");
-    col2im_kernel<<<grid_for(total, 256), 256, 0, as_stream(stream)>>>(dcols_t, dx, g);
+    if (B * C > INT32_MAX || H * W > INT32_MAX || g.Ho * g.Wo > INT32_MAX)
+        return fail(CONCORD_ESHAPE, "concord_col2im: extents above 32-bit indexing");
+    const int64_t per_plane = (H * W + 255) / 256;
+    const dim3 grid((unsigned)(B * C), (unsigned)(per_plane < 64 ? per_plane : 64));
+    cudaStream_t st = as_stream(stream);
+    const bool unit = sh == 1 && sw == 1;
+    if (unit && kh == 3 && kw == 3) col2im_kernel<true, 3, 3><<<grid, 256, 0, st>>>(dcols_t, dx, g);
+    else if (unit && kh == 1 && kw == 1) col2im_kernel<true, 1, 1><<<grid, 256, 0, st>>>(dcols_t, dx, g);
+    else if (unit) col2im_kernel<true, 0, 0><<<grid, 256, 0, st>>>(dcols_t, dx, g);
+    else if (kh == 3 && kw == 3) col2im_kernel<false, 3, 3><<<grid, 256, 0, st>>>(dcols_t, dx, g);
+    else col2im_kernel<false, 0, 0><<<grid, 256, 0, st>>>(dcols_t, dx, g);
     return check_launch("concord_col2im");
 }

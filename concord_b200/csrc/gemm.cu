@@ -12,9 +12,15 @@
 // Each GEMM is a CUTLASS 4 sm100 warp-specialised kernel instantiated here:
 // TMA producer warp -> shared-memory ring -> one thread issuing
 // tcgen05.mma (cta_group::1, 128x256x64 tiles) into TMEM -> epilogue warps
-// reading TMEM with tcgen05.ld and storing through TMA.  Cluster shape 1x1x1:
+// reading TMEM with tcgen05.ld and storing through TMA.  A dW whose N x K
+// output has fewer tiles than the GPU has SMs splits its reduction into
+// slices (a batched GEMM into fp32 partials, summed in slice order and
+// rounded once to bf16).  Cluster shape 1x1x1:
 // every TMA load is a single-CTA load (the same kernels run in multi-GPU jobs).
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
+
+#include <algorithm>
 
 #include "cute/tensor.hpp"
 #include "cutlass/cutlass.h"
@@ -28,7 +34,20 @@
 
 namespace concord {
 int fail(int code, const std::string& msg);
+
+__global__ void splitk_reduce_kernel(const float4* __restrict__ part, uint2* __restrict__ out, int64_t n4, int S) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+        float4 a = part[i];
+        for (int s = 1; s < S; ++s) {
+            const float4 b = part[(int64_t)s * n4 + i];
+            a.x = a.x + b.x; a.y = a.y + b.y; a.z = a.z + b.z; a.w = a.w + b.w;
+        }
+        const __nv_bfloat162 lo = __floats2bfloat162_rn(a.x, a.y);
+        const __nv_bfloat162 hi = __floats2bfloat162_rn(a.z, a.w);
+        out[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+    }
 }
+}  // namespace concord
 
 namespace {
 
@@ -60,23 +79,47 @@ CONCORD_DEFINE_GEMM(GemmFwd, cutlass::layout::RowMajor, cutlass::layout::ColumnM
 CONCORD_DEFINE_GEMM(GemmDx, cutlass::layout::RowMajor, cutlass::layout::RowMajor)
 CONCORD_DEFINE_GEMM(GemmDw, cutlass::layout::ColumnMajor, cutlass::layout::RowMajor)
 
+// dW split over the reduction (M) as a batch of S slices, fp32 partials
+// [S, N, K]; splitk_reduce_kernel sums them in slice order and rounds once.
+using EpiF32 = typename cutlass::epilogue::collective::CollectiveBuilder<
+    cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, TileMNK, Cluster,
+    cutlass::epilogue::collective::EpilogueTileAuto, Acc, Acc, float, LayoutC, 4, float, LayoutC, 4,
+    cutlass::epilogue::TmaWarpSpecialized1Sm>::CollectiveOp;
+using GemmDwSplitMain = typename cutlass::gemm::collective::CollectiveBuilder<
+    cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, BF16, cutlass::layout::ColumnMajor, kAlign, BF16,
+    cutlass::layout::RowMajor, kAlign, Acc, TileMNK, Cluster,
+    cutlass::gemm::collective::StageCountAutoCarveout<static_cast<int>(sizeof(typename EpiF32::SharedStorage))>,
+    cutlass::gemm::KernelTmaWarpSpecialized1SmSm100>::CollectiveOp;
+using GemmDwSplitKernel = cutlass::gemm::kernel::GemmUniversal<Shape<int, int, int, int>, GemmDwSplitMain, EpiF32, void>;
+using GemmDwSplit = cutlass::gemm::device::GemmUniversalAdapter<GemmDwSplitKernel>;
+
+// Slices for dW[N,K] over a reduction of M: only when the N x K output has
+// fewer 128x256 tiles than the GPU has SMs and each slice keeps >= 1024 rows
+// (a multiple of 64); 1 means no split.
+int dw_slices(int64_t M, int64_t N, int64_t K) {
+    const int64_t tiles = ((N + 127) / 128) * ((K + 255) / 256);
+    int S = 1;
+    while (tiles * S * 2 <= 148 * 2 && M % (64 * S * 2) == 0 && M / (S * 2) >= 1024 && S < 16) S *= 2;
+    return tiles >= 148 ? 1 : S;
+}
+
 // D[m,n] = sum_k A[m,k] B[k,n]; strides from the problem's layouts.
-template <class Gemm>
+template <class Gemm, class ElemD = BF16>
 int run_gemm(const void* A, const void* B, void* D, int M, int N, int K, void* workspace, size_t ws_bytes,
-             cudaStream_t stream, bool query_only, size_t* ws_needed, const char* name) {
+             cudaStream_t stream, bool query_only, size_t* ws_needed, const char* name, int L = 1) {
     using StrideA = typename Gemm::GemmKernel::StrideA;
     using StrideB = typename Gemm::GemmKernel::StrideB;
     using StrideC = typename Gemm::GemmKernel::StrideC;
     using StrideD = typename Gemm::GemmKernel::StrideD;
-    StrideA sa = cutlass::make_cute_packed_stride(StrideA{}, cute::make_shape(M, K, 1));
-    StrideB sb = cutlass::make_cute_packed_stride(StrideB{}, cute::make_shape(N, K, 1));
-    StrideC sc = cutlass::make_cute_packed_stride(StrideC{}, cute::make_shape(M, N, 1));
-    StrideD sd = cutlass::make_cute_packed_stride(StrideD{}, cute::make_shape(M, N, 1));
+    StrideA sa = cutlass::make_cute_packed_stride(StrideA{}, cute::make_shape(M, K, L));
+    StrideB sb = cutlass::make_cute_packed_stride(StrideB{}, cute::make_shape(N, K, L));
+    StrideC sc = cutlass::make_cute_packed_stride(StrideC{}, cute::make_shape(M, N, L));
+    StrideD sd = cutlass::make_cute_packed_stride(StrideD{}, cute::make_shape(M, N, L));
     typename Gemm::Arguments args{
-        cutlass::gemm::GemmUniversalMode::kGemm,
-        {M, N, K, 1},
+        L == 1 ? cutlass::gemm::GemmUniversalMode::kGemm : cutlass::gemm::GemmUniversalMode::kBatched,
+        {M, N, K, L},
         {reinterpret_cast<const BF16*>(A), sa, reinterpret_cast<const BF16*>(B), sb},
-        {{1.0f, 0.0f}, reinterpret_cast<const BF16*>(D), sc, reinterpret_cast<BF16*>(D), sd}};
+        {{1.0f, 0.0f}, reinterpret_cast<const ElemD*>(D), sc, reinterpret_cast<ElemD*>(D), sd}};
     Gemm gemm;
     if (query_only) {
         *ws_needed = Gemm::get_workspace_size(args);
@@ -123,8 +166,26 @@ extern "C" int concord_gemm_dw(const uint16_t* dy, const uint16_t* x, uint16_t* 
                                void* workspace, size_t workspace_bytes, void* stream) {
     if (bad(dy) || bad(x) || bad(dw)) return concord::fail(CONCORD_EALIGN, "concord_gemm_dw: null or unaligned pointer");
     if (M <= 0 || N <= 0 || K <= 0) return concord::fail(CONCORD_ESHAPE, "concord_gemm_dw: bad shape");
-    return run_gemm<GemmDw>(dy, x, dw, (int)N, (int)K, (int)M, workspace, workspace_bytes,
-                            reinterpret_cast<cudaStream_t>(stream), false, nullptr, "concord_gemm_dw");
+    const int S = dw_slices(M, N, K);
+    if (S == 1)
+        return run_gemm<GemmDw>(dy, x, dw, (int)N, (int)K, (int)M, workspace, workspace_bytes,
+                                reinterpret_cast<cudaStream_t>(stream), false, nullptr, "concord_gemm_dw");
+    // split-K: slice s reduces rows [s*M/S, (s+1)*M/S) into fp32 partial s at
+    // the start of the workspace; CUTLASS's own workspace follows it
+    const size_t part = (size_t)S * (size_t)N * (size_t)K * sizeof(float);
+    if (workspace_bytes < part || (reinterpret_cast<uintptr_t>(workspace) % 16) != 0)
+        return concord::fail(CONCORD_EWORKSPACE, "concord_gemm_dw: workspace too small for the split reduction");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    int rc = run_gemm<GemmDwSplit, float>(dy, x, workspace, (int)N, (int)K, (int)(M / S),
+                                          static_cast<char*>(workspace) + part, workspace_bytes - part, st, false,
+                                          nullptr, "concord_gemm_dw", S);
+    if (rc) return rc;
+    const int64_t n4 = N * K / 4;
+    concord::splitk_reduce_kernel<<<(unsigned)std::min<int64_t>((n4 + 255) / 256, 148 * 8), 256, 0, st>>>(
+        static_cast<const float4*>(workspace), reinterpret_cast<uint2*>(dw), n4, S);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return concord::fail(CONCORD_ELAUNCH, std::string("concord_gemm_dw: ") + cudaGetErrorString(e));
+    return CONCORD_OK;
 }
 
 extern "C" size_t concord_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
@@ -132,5 +193,12 @@ extern "C" size_t concord_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) 
     run_gemm<GemmFwd>(nullptr, nullptr, nullptr, (int)M, (int)N, (int)K, nullptr, 0, nullptr, true, &a, "");
     run_gemm<GemmDx>(nullptr, nullptr, nullptr, (int)M, (int)K, (int)N, nullptr, 0, nullptr, true, &b, "");
     run_gemm<GemmDw>(nullptr, nullptr, nullptr, (int)N, (int)K, (int)M, nullptr, 0, nullptr, true, &c, "");
+    const int S = dw_slices(M, N, K);
+    if (S > 1) {
+        size_t d = 0;
+        run_gemm<GemmDwSplit, float>(nullptr, nullptr, nullptr, (int)N, (int)K, (int)(M / S), nullptr, 0, nullptr,
+                                     true, &d, "", S);
+        c = std::max(c, (size_t)S * (size_t)N * (size_t)K * sizeof(float) + d);
+    }
     return std::max(a, std::max(b, c));
 }

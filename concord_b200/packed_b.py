@@ -279,6 +279,21 @@ def set_sigmag_sigma(sigma):
         t.fill_(_SIGMAG_SIGMA)
 
 
+# ConcordConv2dPackedB convolution backend: "gemm" (this package's im2col +
+# tcgen05 GEMMs, for shapes whose GEMM extents are multiples of 8) or
+# "cudnn" (torch's conv2d and its grad functions, the reference's route).
+_CONV_BACKEND = "gemm"
+
+
+def set_conv_backend(name):
+    """Choose how ConcordConv2dPackedB runs its convolutions ("gemm" or "cudnn").
+    The packed step is this package's kernels either way."""
+    global _CONV_BACKEND
+    if name not in ("gemm", "cudnn"):
+        raise ValueError(f"conv backend must be 'gemm' or 'cudnn', not {name!r}")
+    _CONV_BACKEND = name
+
+
 def _get_sigmag_sigma(device):
     key = _dev_key(device)
     if key not in _SIGMAG_TENSORS:
@@ -877,7 +892,7 @@ class FusedConcordConv2dPackedB(torch.autograd.Function):
         x_bf16 = x_bf16.contiguous()
         bias_bf16 = (bias.to(torch.bfloat16)
                      if bias is not None and bias.dtype != torch.bfloat16 else bias)
-        ctx.gemm = _gemm.conv_usable(x_bf16, weight_buf, kh, kw, stride, padding)
+        ctx.gemm = _CONV_BACKEND == "gemm" and _gemm.conv_usable(x_bf16, weight_buf, kh, kw, stride, padding)
         if ctx.gemm:
             y = _gemm.conv2d_forward(x_bf16, weight_buf, bias_bf16, kh, kw, stride, padding)
         else:

@@ -109,3 +109,39 @@ def test_conv_layer_step_equals_linear_on_unfolded_input():
         conv.rebalance()
         lin.rebalance()
         assert torch.equal(conv.packed_w, lin.packed_w), t
+
+
+def test_cudnn_backend_switch():
+    """set_conv_backend("cudnn") routes a GEMM-able shape through torch's
+    convolutions; the dW each backend hands to the packed step agrees to bf16
+    rounding (2^-7 of its largest entry), and the layer steps either way."""
+    import concord_b200
+    from concord_b200 import ConcordConv2dPackedB, gemm
+    from concord_b200 import packed_b as pb
+    calls, dws = [], []
+    orig_bwd, orig_step = gemm.conv2d_backward, pb._packed_backward_step
+
+    def spy_bwd(*a):
+        calls.append(1)
+        return orig_bwd(*a)
+
+    def spy_step(ctx, grad_W):
+        dws.append(grad_W.float().clone())
+        return orig_step(ctx, grad_W)
+    gemm.conv2d_backward, pb._packed_backward_step = spy_bwd, spy_step
+    try:
+        for backend in ("cudnn", "gemm"):
+            concord_b200.set_conv_backend(backend)
+            torch.manual_seed(4)
+            c = ConcordConv2dPackedB(16, 32, 3, padding=1, device=DEV, lr=0.01)
+            before = c.packed_w.clone()
+            x = torch.randn(2, 16, 8, 8, device=DEV, requires_grad=True)
+            c(x).float().pow(2).mean().backward()
+            assert not torch.equal(before, c.packed_w)
+        assert len(calls) == 1          # only the "gemm" run used the GEMM path
+        assert (dws[0] - dws[1]).abs().max().item() <= 2.0 ** -7 * dws[1].abs().max().item()
+    finally:
+        gemm.conv2d_backward, pb._packed_backward_step = orig_bwd, orig_step
+        concord_b200.set_conv_backend("gemm")
+    with pytest.raises(ValueError):
+        concord_b200.set_conv_backend("winograd")

@@ -2,14 +2,18 @@
 
 bf16 inputs, fp32 accumulation, bf16 output: the result must equal the fp32
 product up to the bf16 rounding of the output (2^-8 relative) plus a small
-accumulation-order term.
+accumulation-order term.  A dW with fewer output tiles than SMs and a long
+reduction runs split over the reduction (fp32 partials summed in order): same
+bound.
 """
 import pytest
 import torch
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
-SHAPES = [(512, 1280, 1280), (256, 5120, 1280), (384, 1280, 5120), (1024, 10240, 2048), (8, 16, 24)]
+SHAPES = [(512, 1280, 1280), (256, 5120, 1280), (384, 1280, 5120), (1024, 10240, 2048), (8, 16, 24),
+          # long reductions onto small dW outputs: the split-K dW (8, 4 and 2 slices)
+          (8192, 320, 2880), (4096, 64, 1024), (16384, 1280, 1280)]
 
 
 def _close(got, ref):
