@@ -190,6 +190,7 @@ _SIGS = [
      [_P, _I64, _I64, _I64, _I64, _I32, _I32, _I32, _I32, _I32, _I32, _P, _P]),
     ("concord_col2im", ctypes.c_int,
      [_P, _I64, _I64, _I64, _I64, _I32, _I32, _I32, _I32, _I32, _I32, _P, _P]),
+    ("concord_transpose_bf16", ctypes.c_int, [_P, _I64, _I64, _I64, _P, _P]),
 ]
 
 EXPORTED = [s[0] for s in _SIGS]

@@ -129,6 +129,30 @@ __global__ void col2im_kernel(const uint16_t* __restrict__ dcolsT, uint16_t* __r
     }
 }
 
+// Batched bf16 transpose, in [batches, R, C] -> out [batches, C, R]: the
+// NCHW gradient of a convolution as the [B*Ho*Wo, O] rows its dW GEMM reads.
+// 32x32 tiles through shared memory (row pitch 34 halves: the column reads
+// fall on distinct banks), both sides coalesced.
+__global__ void transpose_kernel(const uint16_t* __restrict__ in, uint16_t* __restrict__ out, int64_t R,
+                                 int64_t C) {
+    __shared__ uint16_t tile[32][34];
+    const int64_t b = blockIdx.z;
+    const int64_t r0 = (int64_t)blockIdx.y * 32, c0 = (int64_t)blockIdx.x * 32;
+    const uint16_t* src = in + b * R * C;
+    uint16_t* dst = out + b * R * C;
+#pragma unroll
+    for (int k = 0; k < 32; k += 8) {
+        const int64_t r = r0 + threadIdx.y + k, c = c0 + threadIdx.x;
+        if (r < R && c < C) tile[threadIdx.y + k][threadIdx.x] = src[r * C + c];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < 32; k += 8) {
+        const int64_t c = c0 + threadIdx.y + k, r = r0 + threadIdx.x;
+        if (r < R && c < C) dst[c * R + r] = tile[threadIdx.x][threadIdx.y + k];
+    }
+}
+
 static int make_geom(int64_t B, int64_t C, int64_t H, int64_t W, int32_t kh, int32_t kw, int32_t sh,
                      int32_t sw, int32_t ph, int32_t pw, ConvGeom* g, const char* who) {
     if (B < 0 || C < 0 || H < 0 || W < 0 || kh <= 0 || kw <= 0 || sh <= 0 || sw <= 0 || ph < 0 || pw < 0)
@@ -185,4 +209,16 @@ extern "C" int concord_col2im(const uint16_t* dcols_t, int64_t B, int64_t C, int
     else if (kh == 3 && kw == 3) col2im_kernel<false, 3, 3><<<grid, 256, 0, st>>>(dcols_t, dx, g);
     else col2im_kernel<false, 0, 0><<<grid, 256, 0, st>>>(dcols_t, dx, g);
     return check_launch("concord_col2im");
+}
+
+extern "C" int concord_transpose_bf16(const uint16_t* in, int64_t batches, int64_t R, int64_t C, uint16_t* out,
+                                      void* stream) {
+    if (batches < 0 || R < 0 || C < 0) return fail(CONCORD_EINVAL, "concord_transpose_bf16: negative size");
+    if (batches == 0 || R == 0 || C == 0) return CONCORD_OK;
+    if (!in || !out) return fail(CONCORD_EINVAL, "concord_transpose_bf16: null pointer");
+    if (batches > 65535 || (R + 31) / 32 > 65535 || (C + 31) / 32 > INT32_MAX)
+        return fail(CONCORD_ESHAPE, "concord_transpose_bf16: grid too large");
+    const dim3 grid((unsigned)((C + 31) / 32), (unsigned)((R + 31) / 32), (unsigned)batches);
+    transpose_kernel<<<grid, dim3(32, 8), 0, as_stream(stream)>>>(in, out, R, C);
+    return check_launch("concord_transpose_bf16");
 }

@@ -160,12 +160,15 @@ def conv2d_backward(x, weight_2d, grad_y, kh, kw, stride, padding):
     B, C, H, W = x.shape
     O = weight_2d.shape[0]
     cols, Ho, Wo = _conv_cols(x, kh, kw, stride, padding)
-    gy = grad_y.permute(0, 2, 3, 1).reshape(B * Ho * Wo, O).contiguous()
+    grad_y = grad_y.contiguous()
+    gy = torch.empty(B * Ho * Wo, O, dtype=torch.bfloat16, device=x.device)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)
+    _abi.check(_abi.load().concord_transpose_bf16(_ptr(grad_y), B, O, Ho * Wo, _ptr(gy), stream),
+               "concord_transpose_bf16")
     dW = grad_weight(gy, cols)
     del cols
     dcols_t = forward(weight_2d.t().contiguous(), gy)               # [C*kh*kw, B*Ho*Wo]
     dx = torch.empty(B, C, H, W, dtype=torch.bfloat16, device=x.device)
-    stream = ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)
     _abi.check(_abi.load().concord_col2im(_ptr(dcols_t), *_geom(x, kh, kw, stride, padding), _ptr(dx),
                                           stream), "concord_col2im")
     return dx, dW

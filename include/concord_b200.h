@@ -41,7 +41,8 @@
  *                            (packed_b.py:2081-2106)
  *   concord_gemm_fwd/dx/dw <- F.linear / grad_y @ W / grad_y^T @ x
  *                            (packed_b.py:1219, 1263, 1271-1277)
- *   concord_im2col / concord_col2im <- the data movement inside torch's
+ *   concord_im2col / concord_col2im / concord_transpose_bf16
+ *                         <- the data movement inside torch's
  *                            conv2d / conv2d_input used by the conv layer
  *                            (packed_b.py:2024-2065); with them the conv
  *                            runs on concord_gemm_*
@@ -438,6 +439,11 @@ int concord_im2col(const uint16_t* x, int64_t B, int64_t C, int64_t H, int64_t W
 int concord_col2im(const uint16_t* dcols_t, int64_t B, int64_t C, int64_t H, int64_t W,
                    int32_t kh, int32_t kw, int32_t sh, int32_t sw, int32_t ph, int32_t pw,
                    uint16_t* dx, void* stream);
+/* bf16 out[b][c][r] = in[b][r][c] for in [batches, R, C] (the NCHW
+ * convolution gradient as the [B*Ho*Wo, O] rows of the dW GEMM); batches
+ * <= 65535. */
+int concord_transpose_bf16(const uint16_t* in, int64_t batches, int64_t R, int64_t C, uint16_t* out,
+                           void* stream);
 
 #ifdef __cplusplus
 }

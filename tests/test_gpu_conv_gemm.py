@@ -145,3 +145,17 @@ def test_cudnn_backend_switch():
         concord_b200.set_conv_backend("gemm")
     with pytest.raises(ValueError):
         concord_b200.set_conv_backend("winograd")
+
+
+@pytest.mark.parametrize("shape", [(2, 32, 100), (3, 7, 45), (1, 640, 4096)])
+def test_transpose_bf16(shape):
+    import ctypes
+    from concord_b200 import _abi
+    b, r, c = shape
+    x = torch.randn(b, r, c, device=DEV).to(torch.bfloat16)
+    out = torch.empty(b, c, r, device=DEV, dtype=torch.bfloat16)
+    _abi.check(_abi.load().concord_transpose_bf16(ctypes.c_void_p(x.data_ptr()), b, r, c,
+                                                  ctypes.c_void_p(out.data_ptr()),
+                                                  ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)),
+               "transpose")
+    assert torch.equal(out, x.transpose(1, 2))
