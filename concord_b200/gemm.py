@@ -137,10 +137,36 @@ def conv_usable(x, weight_2d, kh, kw, stride, padding):
     return Ho > 0 and Wo > 0 and IK == C * kh * kw and _ok(B * Ho * Wo, O, IK)
 
 
+def _pointwise(x, kh, kw, stride, padding):
+    """A 1x1, stride-1, unpadded convolution whose per-image GEMMs fit the
+    kernels: each image's NCHW plane [C, H*W] is already a GEMM operand."""
+    return (kh == 1 and kw == 1 and _pair(stride) == (1, 1) and _pair(padding) == (0, 0)
+            and _ok(x.shape[2] * x.shape[3]))
+
+
+def _transpose(t, batches, R, C):
+    out = torch.empty(batches * C, R, dtype=torch.bfloat16, device=t.device)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+    _abi.check(_abi.load().concord_transpose_bf16(_ptr(t), batches, R, C, _ptr(out), stream),
+               "concord_transpose_bf16")
+    return out
+
+
 def conv2d_forward(x, weight_2d, bias, kh, kw, stride, padding):
-    """y = conv2d(x, W) (NCHW, bf16): the forward GEMM of (W, cols)."""
+    """y = conv2d(x, W) (NCHW, bf16): the forward GEMM of (W, cols); for a
+    pointwise convolution y_b = W x_b per image (the dX-layout GEMM), with
+    no column matrix."""
     B = x.shape[0]
     O = weight_2d.shape[0]
+    if _pointwise(x, kh, kw, stride, padding):
+        C, L = x.shape[1], x.shape[2] * x.shape[3]
+        x = x.contiguous()
+        y = torch.empty(B, O, x.shape[2], x.shape[3], dtype=torch.bfloat16, device=x.device)
+        for b in range(B):
+            _run("concord_gemm_dx", weight_2d, x[b], y[b], O, C, L)
+        if bias is not None:
+            y.add_(bias.view(1, O, 1, 1))
+        return y
     cols, Ho, Wo = _conv_cols(x, kh, kw, stride, padding)
     yt = forward(weight_2d, cols)                                  # [O, B*Ho*Wo]
     if B == 1:
@@ -159,12 +185,19 @@ def conv2d_backward(x, weight_2d, grad_y, kh, kw, stride, padding):
     (concord_col2im) and rounds again."""
     B, C, H, W = x.shape
     O = weight_2d.shape[0]
-    cols, Ho, Wo = _conv_cols(x, kh, kw, stride, padding)
     grad_y = grad_y.contiguous()
-    gy = torch.empty(B * Ho * Wo, O, dtype=torch.bfloat16, device=x.device)
+    if _pointwise(x, kh, kw, stride, padding):
+        L = H * W
+        x = x.contiguous()
+        dW = grad_weight(_transpose(grad_y, B, O, L), _transpose(x, B, C, L))
+        wt = weight_2d.t().contiguous()
+        dx = torch.empty(B, C, H, W, dtype=torch.bfloat16, device=x.device)
+        for b in range(B):                     # dx_b = W^T dy_b: one rounding per pixel
+            _run("concord_gemm_dx", wt, grad_y[b], dx[b], C, O, L)
+        return dx, dW
+    cols, Ho, Wo = _conv_cols(x, kh, kw, stride, padding)
+    gy = _transpose(grad_y, B, O, Ho * Wo)
     stream = ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)
-    _abi.check(_abi.load().concord_transpose_bf16(_ptr(grad_y), B, O, Ho * Wo, _ptr(gy), stream),
-               "concord_transpose_bf16")
     dW = grad_weight(gy, cols)
     del cols
     dcols_t = forward(weight_2d.t().contiguous(), gy)               # [C*kh*kw, B*Ho*Wo]
