@@ -399,6 +399,10 @@ namespace concord {
 constexpr int STEP_THREADS = 256;
 constexpr int VEC = 4;                 // consecutive columns per thread
 constexpr int STEP_COLS = 32 * VEC;    // columns per block (one warp-width)
+#ifndef CONCORD_STEP_LOCK
+#define CONCORD_STEP_LOCK 2
+#endif
+constexpr int STEP_LOCK = CONCORD_STEP_LOCK;  // elements computed in lockstep (divides VEC)
 constexpr int STEP_ROWS = 64;          // rows per block (8 per warp); fewer on small layers
 
 __device__ __forceinline__ void block_add_coh(double csum, double ccnt, double* coh_stats) {
@@ -515,25 +519,33 @@ __global__ void __launch_bounds__(STEP_THREADS, MINB) step_vec_kernel(StepArgs A
                                                       posn ^ (int32_t)(k0 + j));
                 }
             } else if (KIND == CONCORD_KIND_ADAMW) {
-                // phase 1: up to the denominator's argument; phase 2: the four
-                // correctly rounded exp2(p*log2(x)) side by side; phase 3: the rest
-                AdamwPre pre[VEC];
-                float xs[VEC], den[VEC];
+                // LOCK elements at a time: phase 1 up to the denominator's
+                // argument; phase 2 the correctly rounded exp2(p*log2(x)) side by
+                // side; phase 3 the rest
 #pragma unroll
-                for (int j = 0; j < VEC; ++j) {
-                    const float g = bf16_to_f32((gw[j >> 1] >> ((j & 1) * 16)) & 0xffffu);
-                    pre[j] = adamw_pre<FL, true>(A.P, wv[j], g, re, ce[j], vr, vc[j], cp[j], S);
-                    xs[j] = pre[j].x;
+                for (int h = 0; h < VEC; h += STEP_LOCK) {
+                    AdamwPre pre[STEP_LOCK];
+                    float xs[STEP_LOCK], den[STEP_LOCK];
+                    ElemOut o2[STEP_LOCK];
+#pragma unroll
+                    for (int u = 0; u < STEP_LOCK; ++u) {
+                        const int j = h + u;
+                        const float g = bf16_to_f32((gw[j >> 1] >> ((j & 1) * 16)) & 0xffffu);
+                        pre[u] = adamw_pre<FL, true>(A.P, wv[j], g, re, ce[j], vr, vc[j], cp[j], S);
+                        xs[u] = pre[u].x;
+                    }
+#pragma unroll
+                    for (int u = 0; u < STEP_LOCK; ++u) fixed_coh_divide<FL>(A.P, pre[u]);
+                    crmath::cr_pow2log2<STEP_LOCK>(xs, A.P.precond_p, den);
+#pragma unroll
+                    for (int u = 0; u < STEP_LOCK; ++u) den[u] = pre[u].g / den[u];
+                    int32_t posv[STEP_LOCK];
+#pragma unroll
+                    for (int u = 0; u < STEP_LOCK; ++u) posv[u] = posn ^ (int32_t)(k0 + h + u);
+                    adamw_post_lockstep<FL, STEP_LOCK>(A.P, pre, den, S, posv, o2);
+#pragma unroll
+                    for (int u = 0; u < STEP_LOCK; ++u) outs[h + u] = o2[u];
                 }
-#pragma unroll
-                for (int j = 0; j < VEC; ++j) fixed_coh_divide<FL>(A.P, pre[j]);
-                crmath::cr_pow2log2<VEC>(xs, A.P.precond_p, den);
-#pragma unroll
-                for (int j = 0; j < VEC; ++j) den[j] = pre[j].g / den[j];
-                int32_t posv[VEC];
-#pragma unroll
-                for (int j = 0; j < VEC; ++j) posv[j] = posn ^ (int32_t)(k0 + j);
-                adamw_post_lockstep<FL, VEC>(A.P, pre, den, S, posv, outs);
             } else {
 #pragma unroll
                 for (int j = 0; j < VEC; ++j) {
