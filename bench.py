@@ -134,7 +134,7 @@ def make_grads(n_rows, k_cols, device, count=2, seed=1):
 
 
 SHARDED = None
-STEP_TRAFFIC_PER_PARAM = (83.997696e6 + 51.58272e6) / (4096 * 2048)
+STEP_TRAFFIC_PER_PARAM = (84.079872e6 + 53.77408e6) / (4096 * 2048)
 
 
 def optimizer_step(layer, grad, coh_stats=None, ev=None):
