@@ -137,7 +137,27 @@ __device__ __forceinline__ void reb_shift_word(const RebArgs& A, int64_t n, int6
 }
 
 // Touches only words of a ticked row or a ticked column: first every column of
-// the ticked rows, then every other row of the ticked columns.
+// the ticked rows, then every other row of the ticked columns.  The index
+// arithmetic runs in 32 bits when the work fits (it does unless a layer
+// holds 2^31 words).
+template <typename I>
+__device__ __forceinline__ void reb_shift_range(const RebArgs& A, int64_t nr64, int64_t nc64, int32_t sd,
+                                                uint32_t NK) {
+    const I K = (I)A.K, nc = (I)nc64;
+    const I rows_work = (I)nr64 * K, total = rows_work + (I)A.N * nc;
+    for (I i = (I)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (I)gridDim.x * blockDim.x) {
+        if (i < rows_work) {
+            const I r = i / K;
+            reb_shift_word(A, A.rowlist[r], (int64_t)(i - r * K), sd, NK);
+        } else {
+            const I j = i - rows_work;
+            const I n = j / nc;
+            if (A.rt[n] != 0) continue;  // done in the row pass
+            reb_shift_word(A, (int64_t)n, A.collist[j - n * nc], sd, NK);
+        }
+    }
+}
+
 __global__ void reb_shift_kernel(RebArgs A) {
     const int32_t fired = A.fired[0];
     if (A.fired_out && blockIdx.x == 0 && threadIdx.x == 0) *A.fired_out = fired;
@@ -145,19 +165,11 @@ __global__ void reb_shift_kernel(RebArgs A) {
     const int32_t sd = *A.seed;
     const uint32_t NK = (uint32_t)(A.N_total * A.K);
     const int64_t nr = A.fired[1], nc = A.fired[2];
-    const int64_t rows_work = nr * A.K, total = rows_work + A.N * nc;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        if (i < rows_work) {
-            const int64_t n = A.rowlist[i / A.K];
-            reb_shift_word(A, n, i % A.K, sd, NK);
-        } else {
-            const int64_t j = i - rows_work;
-            const int64_t n = j / nc;
-            if (A.rt[n] != 0) continue;  // done in the row pass
-            reb_shift_word(A, n, A.collist[j % nc], sd, NK);
-        }
-    }
+    const int64_t total = nr * A.K + A.N * nc;
+    if (total + (int64_t)gridDim.x * blockDim.x < ((int64_t)1 << 31))
+        reb_shift_range<uint32_t>(A, nr, nc, sd, NK);
+    else
+        reb_shift_range<int64_t>(A, nr, nc, sd, NK);
 }
 
 // ---------------------------------------------------------------------------
