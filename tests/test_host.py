@@ -35,6 +35,19 @@ def test_library_exports_header_symbols(built):
     assert _abi.load().concord_abi_version() == 2
 
 
+def test_gemm_dw_split_decision(built):
+    """A dW with fewer output tiles than SMs and a long reduction reserves
+    fp32 partials for its split (S * N * K * 4 bytes of workspace); the C2
+    Linear shapes do not split."""
+    from concord_b200 import _abi
+    ws = _abi.load().concord_gemm_workspace_bytes
+    assert ws(8192, 320, 2880) >= 8 * 320 * 2880 * 4       # 36 tiles: 8 slices
+    assert ws(4096, 64, 1024) >= 4 * 64 * 1024 * 4         # 4 tiles, 1024-row slices
+    assert ws(16384, 1280, 1280) >= 2 * 1280 * 1280 * 4    # 50 tiles: 2 slices
+    assert ws(512, 1280, 1280) < 1280 * 1280 * 4           # reduction too short
+    assert ws(8192, 10240, 2048) < 10240 * 2048 * 4        # 640 tiles
+
+
 def test_crmath_host_matches_extended_precision(built):
     lib = ctypes.CDLL(os.path.join(ROOT, "concord_b200", "_lib", "libcrmath_check.so"))
     rng = np.random.default_rng(1)
