@@ -21,6 +21,8 @@ from .packed_b import (  # noqa: F401
     set_conv_backend,
     reset_reb_stats,
     get_reb_stats,
+    set_arithmetic,
+    get_arithmetic,
     gate_coherence_from_fields,
     measure_coherence,
     DissipationAutoTuner,
@@ -43,6 +45,8 @@ __all__ = [
     "set_gate_gain",
     "reset_reb_stats",
     "get_reb_stats",
+    "set_arithmetic",
+    "get_arithmetic",
     "set_conv_backend",
     "S_SLOW_FACTOR",
     "V_SLOW_FACTOR",

@@ -8,7 +8,7 @@ import ctypes
 import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-ABI_VERSION = 2   # CONCORD_ABI_VERSION of include/concord_b200.h
+ABI_VERSION = 3   # CONCORD_ABI_VERSION of include/concord_b200.h
 LIB_PATH = os.path.join(_HERE, "_lib", "libconcord_b200.so")
 
 # flag bits (packed_b.py:451-458 constexprs)
@@ -23,6 +23,10 @@ F_RATIO_COH = 1 << 7
 
 KIND_ADAMW = 0
 KIND_SGD = 1
+
+# fp32 arithmetic of the step (CONCORD_ARITH_*)
+ARITH_GPU = 0
+ARITH_CR = 1
 
 PEER_SUM_F32 = 0
 PEER_MAX_I32 = 1
@@ -66,6 +70,7 @@ class StepParams(ctypes.Structure):
         ("alpha_gate_gain", ctypes.c_float),
         ("consolidate", ctypes.c_void_p),
         ("ratio_floors", ctypes.c_void_p),
+        ("arith", ctypes.c_int32),
     ]
 
 
@@ -75,14 +80,16 @@ def make_step_params(kind="adamw", mantissa_bias=15, alpha=0.1, beta1=0.0,
                      wd_sv=0.0, wd_sf=0.0, gf_trust_delta_sq=0.0, gate_gain=1.0,
                      chase_floor=0.9, leak_floor=0.999, mass_preserve=False,
                      apply_chase=True, track_rebalance=True, use_cohpre=False,
-                     fixed_coh=True, ratio_coh=False):
+                     fixed_coh=True, ratio_coh=False, arith=ARITH_GPU):
     """Build the launch scalars the way the reference's launch computes them.
 
     Flags follow apply_packed_adamw (packed_b.py:897-899, 943-950): the trust
     region is on iff gf_trust_delta_sq > 0, evaporation iff gf_consol > 0.
     Scalars that the reference combines on the host before they meet a tensor
     (`1.0 - alpha_v_fast`, `1.0 - chase_floor`, `alpha * 1.0 * gate_gain`) are
-    combined here in double and rounded once to fp32 by ctypes.
+    combined here in double and rounded once to fp32 by ctypes (used by the
+    ARITH_CR model; ARITH_GPU recombines them in fp32 as the compiled
+    reference does).
     """
     flags = 0
     if mass_preserve:
@@ -115,6 +122,7 @@ def make_step_params(kind="adamw", mantissa_bias=15, alpha=0.1, beta1=0.0,
         chase_floor=float(chase_floor), one_minus_chase_floor=1.0 - float(chase_floor),
         leak_floor=float(leak_floor), one_minus_leak_floor=1.0 - float(leak_floor),
         alpha_gate_gain=alpha * 1.0 * float(gate_gain),
+        arith=int(arith),
     )
 
 
@@ -176,12 +184,14 @@ _SIGS = [
     ("concord_rebalance_workspace_bytes", ctypes.c_size_t, [_I64, _I64]),
     ("concord_rebalance", ctypes.c_int,
      [_P, _I64, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32,
-      _I64, _I64, _I64, _I64, _P, _P, ctypes.c_size_t, _P]),
+      _I64, _I64, _I64, _I64, _P, _P, _P, ctypes.c_size_t, _P]),
     ("concord_materialize", ctypes.c_int,
      [_P, _I64, _P, _P, _P, _I64, _I64, _I64, _I32, _I32, _P]),
     ("concord_quantize", ctypes.c_int,
      [_P, _I64, _P, _I64, _P, _P, _I64, _I64, _I32, _I32, _I32, _I32, _P]),
     ("concord_coherence", ctypes.c_int, [_P, _I64, _I64, _I64, _F, _P, _P]),
+    ("concord_garbage_fraction", ctypes.c_int,
+     [_P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I32, _F, _P, _P, _P]),
     ("concord_gemm_workspace_bytes", ctypes.c_size_t, [_I64, _I64, _I64]),
     ("concord_gemm_fwd", ctypes.c_int, [_P, _P, _P, _I64, _I64, _I64, _P, ctypes.c_size_t, _P]),
     ("concord_gemm_dx", ctypes.c_int, [_P, _P, _P, _I64, _I64, _I64, _P, ctypes.c_size_t, _P]),

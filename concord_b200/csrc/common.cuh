@@ -68,6 +68,27 @@ __device__ __forceinline__ float hash_uniform(int32_t x, int32_t pos, int32_t sa
     return __int2float_rn(h & 0xFFFFFF) * (1.0f / 16777216.0f);
 }
 
+// ---- the reference's arithmetic as compiled for NVIDIA GPUs ----
+// The reference's kernels are Triton; compiled for sm_100 its fp32 `/` is the
+// PTX full-range approximate division, tl.exp2 the hardware approximation
+// ex2.approx, tl.log2 the CUDA math library's log2f, and a multiply feeding an
+// add is contracted into one fma at the sites the step kernel spells out.
+// These were identified by comparing outputs with the compiled reference
+// on a B200 (every case of the step bit-identical), not by reading any
+// compiled code.
+__device__ __forceinline__ float div_full(float a, float b) {
+    float r;
+    asm("div.full.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ float ex2_approx(float x) {
+    float r;
+    asm("ex2.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+// tl.minimum(tl.maximum(x, lo), hi) as compiled: NaN operands are dropped
+__device__ __forceinline__ float clamp_gpu(float x, float lo, float hi) { return fminf(fmaxf(x, lo), hi); }
+
 // SR tick: floor(d) + (r < frac(d)) truncated to int32 (packed_b.py:596-598)
 __device__ __forceinline__ int32_t sr_tick(float d, float r) {
     float fl = floorf(d);

@@ -103,6 +103,22 @@ int dw_slices(int64_t M, int64_t N, int64_t K) {
     return tiles >= 148 ? 1 : S;
 }
 
+// The TMA descriptors are encoded through the driver API, which needs a
+// current context on the calling host thread.  A thread whose first CUDA work
+// is this call (an autograd worker thread running a backward whose first node
+// is this layer, for instance) may have none bound yet; encoding then fails
+// and the kernel would run with an invalid descriptor.  Binding the current
+// device's primary context first (cudaSetDevice of the device already current)
+// rules that out without changing the caller's device.
+int bind_current_context(const char* name) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaSetDevice(dev);
+    if (e != cudaSuccess)
+        return concord::fail(CONCORD_ENODEVICE, std::string(name) + ": no usable CUDA device: " + cudaGetErrorString(e));
+    return CONCORD_OK;
+}
+
 // D[m,n] = sum_k A[m,k] B[k,n]; strides from the problem's layouts.
 template <class Gemm, class ElemD = BF16>
 int run_gemm(const void* A, const void* B, void* D, int M, int N, int K, void* workspace, size_t ws_bytes,
@@ -130,6 +146,7 @@ int run_gemm(const void* A, const void* B, void* D, int M, int N, int K, void* w
                                              "(every extent must be a multiple of 8)");
     if (Gemm::get_workspace_size(args) > ws_bytes)
         return concord::fail(CONCORD_EWORKSPACE, std::string(name) + ": workspace too small");
+    if (int rc = bind_current_context(name)) return rc;
     if (gemm.initialize(args, workspace, stream) != cutlass::Status::kSuccess)
         return concord::fail(CONCORD_ELAUNCH, std::string(name) + ": initialize failed");
     if (gemm.run(stream) != cutlass::Status::kSuccess)

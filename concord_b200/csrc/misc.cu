@@ -129,6 +129,53 @@ __global__ void coherence_kernel(const int32_t* packed, int64_t ldp, int64_t N, 
     }
 }
 
+// Per-weight garbage fraction (get_garbage_fraction_stats, packed_b.py:1676-1730):
+// gf = clamp((noise * 2^te)^2 / (v_hat + 1e-30), 0, 1) with noise the
+// drift-cancelled velocity s_fast - C * (128 s_slow - 128 v_slow) and
+// v_hat = v_row v_col / sum_v, every operation one fp32 rounding as torch
+// evaluates it.  gf is written when gf_out is given; acc[0..2] += sum of gf,
+// count of gf < 0.1, count of gf > 0.9 (double, one atomic per block).
+__global__ void garbage_fraction_kernel(const int32_t* packed, int64_t ldp, const int8_t* row_exp,
+                                        const int8_t* col_exp, const float* v_row, const float* v_col,
+                                        const float* sum_v, int64_t N, int64_t K, int32_t mb, float C,
+                                        float* gf_out, double* acc) {
+    __shared__ double red[3][8];
+    const float sv = *sum_v;
+    double a0 = 0.0, a1 = 0.0, a2 = 0.0;
+    const int64_t total = N * K;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t n = i / K, k = i - n * K;
+        const int32_t w = packed[n * ldp + k];
+        const float sf = (float)(w >> 16);
+        const float ssf = __fmul_rn((float)(shl32(w, 16) >> 24), 128.0f);
+        const float vsf = __fmul_rn((float)(shl32(w, 24) >> 24), 128.0f);
+        const float noise = __fsub_rn(sf, __fmul_rn(C, __fsub_rn(ssf, vsf)));
+        const float nw = __fmul_rn(noise, exp2i((int32_t)row_exp[n] + (int32_t)col_exp[k] - mb));
+        const float vh = __fdiv_rn(__fmul_rn(v_row[n], v_col[k]), sv);
+        float gf = __fdiv_rn(__fmul_rn(nw, nw), __fadd_rn(vh, 1e-30f));
+        gf = fminf(fmaxf(gf, 0.0f), 1.0f);
+        if (gf_out) gf_out[i] = gf;
+        a0 += (double)gf;
+        a1 += gf < 0.1f ? 1.0 : 0.0;
+        a2 += gf > 0.9f ? 1.0 : 0.0;
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        a0 += __shfl_xor_sync(0xffffffffu, a0, o);
+        a1 += __shfl_xor_sync(0xffffffffu, a1, o);
+        a2 += __shfl_xor_sync(0xffffffffu, a2, o);
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) { red[0][warp] = a0; red[1][warp] = a1; red[2][warp] = a2; }
+    __syncthreads();
+    if (threadIdx.x < 3) {
+        double t = 0.0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[threadIdx.x][w];
+        atomicAdd(acc + threadIdx.x, t);
+    }
+}
+
 __global__ void salt_bump_kernel(int32_t* salt) { *salt += 1; }
 
 static unsigned grid_for(int64_t total, int threads) {
@@ -190,4 +237,17 @@ extern "C" int concord_coherence(const int32_t* packed, int64_t ldp, int64_t N, 
     if (N == 0 || K == 0) return CONCORD_OK;
     coherence_kernel<<<grid_for(N * K, 256), 256, 0, as_stream(stream)>>>(packed, ldp, N, K, drift_cancel_C, out);
     return check_launch("concord_coherence");
+}
+
+extern "C" int concord_garbage_fraction(const int32_t* packed, int64_t ldp, const int8_t* row_exp,
+                                        const int8_t* col_exp, const float* v_row, const float* v_col,
+                                        const float* sum_v, int64_t N, int64_t K, int32_t mantissa_bias,
+                                        float drift_cancel_C, float* gf_out, double* acc, void* stream) {
+    if (!packed || !row_exp || !col_exp || !v_row || !v_col || !sum_v || !acc)
+        return fail(CONCORD_EINVAL, "concord_garbage_fraction: null pointer");
+    if (N < 0 || K < 0 || ldp < K) return fail(CONCORD_ESHAPE, "concord_garbage_fraction: bad shape/stride");
+    if (N == 0 || K == 0) return CONCORD_OK;
+    garbage_fraction_kernel<<<grid_for(N * K, 256), 256, 0, as_stream(stream)>>>(
+        packed, ldp, row_exp, col_exp, v_row, v_col, sum_v, N, K, mantissa_bias, drift_cancel_C, gf_out, acc);
+    return check_launch("concord_garbage_fraction");
 }

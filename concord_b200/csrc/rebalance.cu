@@ -35,6 +35,7 @@ struct RebArgs {
     int8_t* rt; int8_t* ct; int32_t* fired;   // fired[0] flag, [1] #rows, [2] #cols ticked
     int32_t* rhist; int32_t* chist;
     int32_t* rowlist; int32_t* collist;       // rows / columns whose exponent moved
+    unsigned long long* stats;                // optional: [tick-ups, tick-downs, clipped words]
 };
 
 __global__ void reb_hist_kernel(RebArgs A) {
@@ -79,6 +80,7 @@ __global__ void reb_decide_kernel(RebArgs A) {
             dn = mx <= A.max_m && med <= 31 && e > A.exp_min;
         }
         const int t = up - dn;
+        if (A.stats && t) atomicAdd(A.stats + (up ? 0 : 1), 1ull);
         A.rt[n] = (int8_t)t;
         if (t) {
             A.row_exp[n] = (int8_t)(e + t);
@@ -97,6 +99,7 @@ __global__ void reb_decide_kernel(RebArgs A) {
             dn = mx <= A.max_m && med <= 31 && e > A.exp_min;
         }
         const int t = up - dn;
+        if (A.stats && t) atomicAdd(A.stats + (up ? 0 : 1), 1ull);
         A.ct[k] = (int8_t)t;
         if (t) {
             A.col_exp[k] = (int8_t)(e + t);
@@ -104,6 +107,25 @@ __global__ void reb_decide_kernel(RebArgs A) {
             A.collist[atomicAdd(A.fired + 2, 1)] = (int32_t)k;
         }
     }
+}
+
+// Diagnostic (only with stats): words whose larger int8 field no longer fits
+// in int8 once the net left shift of a tick-down is applied,
+// max(|s_slow|, |v_slow|) << max(0, -(rt + ct)) > 127, counted on the
+// pre-shift words (a field of -128 counts even without a shift).
+__global__ void reb_clip_count_kernel(RebArgs A) {
+    unsigned long long c = 0;
+    const int64_t total = A.N * A.K;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t n = i / A.K, k = i - n * A.K;
+        const int32_t w = A.packed[n * A.ldp + k];
+        const int32_t m = max(abs(shl32(w, 16) >> 24), abs(shl32(w, 24) >> 24));
+        const int32_t lsh = max(0, -((int32_t)A.rt[n] + (int32_t)A.ct[k]));
+        c += (m << lsh) > 127;
+    }
+    for (int o = 16; o >= 1; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+    if ((threadIdx.x & 31) == 0 && c) atomicAdd(A.stats + 2, c);
 }
 
 __device__ __forceinline__ void reb_shift_word(const RebArgs& A, int64_t n, int64_t k, int32_t sd, uint32_t NK) {
@@ -201,7 +223,7 @@ __device__ __forceinline__ RebArgs reb_args_of(const concord_reb_layer& L) {
     A.seed = L.seed; A.max_m = L.max_m; A.exp_max = L.exp_max; A.exp_min = L.exp_min; A.allow_td = 0;
     A.N = L.N; A.K = L.K; A.row0 = L.row0; A.N_total = L.N_total; A.fired_out = nullptr;
     A.rt = L.rt; A.ct = L.ct; A.fired = L.fired; A.rhist = nullptr; A.chist = nullptr;
-    A.rowlist = L.rowlist; A.collist = L.collist;
+    A.rowlist = L.rowlist; A.collist = L.collist; A.stats = nullptr;
     return A;
 }
 
@@ -343,8 +365,9 @@ extern "C" int concord_rebalance(int32_t* packed, int64_t ldp, int8_t* row_exp, 
                                  const int32_t* row_max, const int32_t* col_max, int32_t* row_hwm,
                                  int32_t* col_hwm, int32_t* seed, int32_t max_m, int32_t exp_max,
                                  int32_t exp_min, int32_t allow_tickdown, int64_t N, int64_t K,
-                                 int64_t row0, int64_t N_total, int32_t* fired_out, void* workspace,
-                                 size_t workspace_bytes, void* stream) {
+                                 int64_t row0, int64_t N_total, int32_t* fired_out,
+                                 unsigned long long* stats, void* workspace, size_t workspace_bytes,
+                                 void* stream) {
     if (!packed || !row_exp || !col_exp || !row_max || !col_max || !seed)
         return fail(CONCORD_EINVAL, "concord_rebalance: null pointer");
     if (N <= 0 || K <= 0 || ldp < K || row0 < 0 || N_total < row0 + N)
@@ -361,6 +384,7 @@ extern "C" int concord_rebalance(int32_t* packed, int64_t ldp, int8_t* row_exp, 
     A.seed = seed; A.max_m = max_m; A.exp_max = exp_max; A.exp_min = exp_min;
     A.allow_td = allow_tickdown; A.N = N; A.K = K; A.row0 = row0; A.N_total = N_total;
     A.fired_out = fired_out;
+    A.stats = stats;
     A.fired = reinterpret_cast<int32_t*>(ws);
     A.rt = reinterpret_cast<int8_t*>(ws + 256);
     A.ct = reinterpret_cast<int8_t*>(ws + 256 + al256((size_t)N));
@@ -372,8 +396,14 @@ extern "C" int concord_rebalance(int32_t* packed, int64_t ldp, int8_t* row_exp, 
     if (cudaMemsetAsync(A.fired, 0, 3 * sizeof(int32_t), s) != cudaSuccess) return check_launch("concord_rebalance");
     int64_t blocks = (N * K + RB_THREADS - 1) / RB_THREADS;
     if (blocks > 148 * 32) blocks = 148 * 32;
+    // the histogram bins sit at shape-dependent offsets of a workspace that
+    // callers may share between layers of different shapes: clear them first
+    if (allow_tickdown &&
+        cudaMemsetAsync(A.rhist, 0, al256((size_t)N * HB * 4) + (size_t)K * HB * 4, s) != cudaSuccess)
+        return check_launch("concord_rebalance");
     if (allow_tickdown) reb_hist_kernel<<<(unsigned)blocks, RB_THREADS, 0, s>>>(A);
     reb_decide_kernel<<<(unsigned)((N + K + RB_THREADS - 1) / RB_THREADS), RB_THREADS, 0, s>>>(A);
+    if (stats) reb_clip_count_kernel<<<(unsigned)blocks, RB_THREADS, 0, s>>>(A);
     reb_shift_kernel<<<148 * 4, RB_THREADS, 0, s>>>(A);
     return check_launch("concord_rebalance");
 }

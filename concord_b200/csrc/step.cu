@@ -47,6 +47,9 @@ constexpr uint32_t FL_ZERO_WD = 0x40000000u;
 // With the exponent range of a SAFE row (|te| <= 46, so every product below is
 // finite) the terms they scale are exact no-ops for the ticks.
 constexpr uint32_t FL_PLAIN = 0x20000000u;
+// set in an instantiation's flag word: the reference-GPU arithmetic
+// (CONCORD_ARITH_GPU); FL_DYNAMIC instantiations read P.arith instead
+constexpr uint32_t FL_GPU = 0x10000000u;
 constexpr uint32_t FL_BARE = CONCORD_F_MASS_PRESERVE | CONCORD_F_APPLY_CHASE | CONCORD_F_TRACK_REBALANCE |
                              CONCORD_F_GF_TRUST | CONCORD_F_COHPRE | CONCORD_F_FIXED_COH | FL_ZERO_WD | FL_PLAIN;
 constexpr uint32_t FL_NOCOHPRE = FL_BARE & ~CONCORD_F_COHPRE;
@@ -54,6 +57,21 @@ constexpr uint32_t FL_NOCOHPRE = FL_BARE & ~CONCORD_F_COHPRE;
 template <uint32_t FL>
 __device__ __forceinline__ uint32_t flags_of(const concord_step_params& P) {
     return (FL & FL_DYNAMIC) ? P.flags : (FL & 0xffffu);
+}
+
+template <uint32_t FL>
+__device__ __forceinline__ bool gpu_of(const concord_step_params& P) {
+    return (FL & FL_DYNAMIC) ? P.arith == CONCORD_ARITH_GPU : (FL & FL_GPU) != 0;
+}
+
+// a * b + c rounded as the chosen arithmetic does: one fma (GPU) or two roundings (CR)
+__device__ __forceinline__ float mad_as(bool gpu, float a, float b, float c) {
+    return gpu ? __fmaf_rn(a, b, c) : __fadd_rn(__fmul_rn(a, b), c);
+}
+
+// denominator exp2(p * log2(x)) of the chosen arithmetic (one element)
+__device__ __forceinline__ float pow2log2_as(bool gpu, float p, float x) {
+    return gpu ? ex2_approx(__fmul_rn(p, log2f(x))) : crmath::cr_exp2f(p * crmath::cr_log2f(x));
 }
 
 // First half of one AdamW-path element (packed_b.py:476-557): everything up
@@ -75,6 +93,7 @@ __device__ __forceinline__ AdamwPre adamw_pre(const concord_step_params& P, int3
                                               int32_t row_e, int32_t col_e, float v_row, float v_col,
                                               float cp, const StepScalars& S) {
     const uint32_t F = flags_of<FL>(P);
+    const bool gpu = gpu_of<FL>(P);
     AdamwPre e;
     e.s_fast = packed >> 16;
     e.s_slow = shl32(packed, 16) >> 24;
@@ -85,7 +104,7 @@ __device__ __forceinline__ AdamwPre adamw_pre(const concord_step_params& P, int3
     const float scale_fwd = pow2_exp<SAFE>(e.te);
     e.d_fs = (float)e.s_fast;
     const float d_sv = (float)(e.s_slow * 128 - e.v_slow * 128);
-    const float noise = e.d_fs - P.drift_cancel_C * d_sv;
+    const float noise = gpu ? __fmaf_rn(-P.drift_cancel_C, d_sv, e.d_fs) : e.d_fs - P.drift_cancel_C * d_sv;
     const float noise_in_w = noise * scale_fwd;
     const bool plain = SAFE && (FL & FL_PLAIN);
     // v_scale == 0: noise_in_w^2 * 0 == +0 (finite for SAFE rows)
@@ -96,18 +115,21 @@ __device__ __forceinline__ AdamwPre adamw_pre(const concord_step_params& P, int3
     if (need_vhat) v_hat = v_row * v_col * S.svi;
     // delta_sq == 1 and v_hat >= +0: 0 + 1 * v_hat == v_hat
     if (plain) v_proxy = v_hat;
-    else if (F & CONCORD_F_GF_TRUST) v_proxy = v_proxy + P.gf_trust_delta_sq * v_hat;
+    else if (F & CONCORD_F_GF_TRUST) v_proxy = gpu ? __fmaf_rn(P.gf_trust_delta_sq, v_hat, v_proxy)
+                                                   : v_proxy + P.gf_trust_delta_sq * v_hat;
     if (need_coh) {
         if (F & CONCORD_F_FIXED_COH) {
             const float sig_w = P.drift_cancel_C * d_sv * scale_fwd;
             const float sig2 = sig_w * sig_w;
             // 0 <= sig2 <= den: the reference's clamp is the identity (NaN propagates)
             e.coh_num = sig2;
-            e.coh_den = sig2 + noise_in_w * noise_in_w + 1e-30f;
+            e.coh_den = gpu ? __fmaf_rn(sig_w, sig_w, noise_in_w * noise_in_w) + 1e-30f
+                            : sig2 + noise_in_w * noise_in_w + 1e-30f;
             coh = 0.0f;  // = coh_num / coh_den, see fixed_coh_divide
         } else {
             const float mg = P.alpha_v_fast * d_sv * scale_fwd;
-            coh = np_min(np_max(mg * mg / (v_hat + 1e-12f), 0.0f), 1.0f);
+            coh = gpu ? clamp_gpu(div_full(mg * mg, v_hat + 1e-12f), 0.0f, 1.0f)
+                      : np_min(np_max(mg * mg / (v_hat + 1e-12f), 0.0f), 1.0f);
         }
     }
     e.coh = coh;
@@ -121,7 +143,7 @@ template <uint32_t FL>
 __device__ __forceinline__ void fixed_coh_divide(const concord_step_params& P, AdamwPre& e) {
     const uint32_t F = flags_of<FL>(P);
     if ((F & (CONCORD_F_GF_CONSOL | CONCORD_F_COHPRE | CONCORD_F_RATIO_COH)) && (F & CONCORD_F_FIXED_COH))
-        e.coh = e.coh_num / e.coh_den;
+        e.coh = gpu_of<FL>(P) ? clamp_gpu(div_full(e.coh_num, e.coh_den), 0.0f, 1.0f) : e.coh_num / e.coh_den;
 }
 
 // Second half (packed_b.py:558-703), given denom_p = exp2(p*log2(x)).
@@ -129,25 +151,30 @@ template <uint32_t FL, bool SAFE = false>
 __device__ __forceinline__ ElemOut adamw_post(const concord_step_params& P, const AdamwPre& e,
                                               float step_div, const StepScalars& S, int32_t pos) {
     const uint32_t F = flags_of<FL>(P);
+    const bool gpu = gpu_of<FL>(P);
     const float scale_fwd = pow2_exp<SAFE>(e.te);
     const float scale_inv = pow2_exp<SAFE>(-e.te);
     const float coh = e.coh, d_fs = e.d_fs;
     int32_t s_fast = e.s_fast, s_slow = e.s_slow;
     const int32_t v_slow = e.v_slow;
-    float step_live = clamp_np(step_div, P.step_cap);  // step_div = g / denom_p
+    // step_div = g / denom_p
+    float step_live = gpu ? clamp_gpu(step_div, -P.step_cap, P.step_cap) : clamp_np(step_div, P.step_cap);
     const bool consol = (F & CONCORD_F_GF_CONSOL) != 0;
-    float evap = 0.0f;
+    float evap_rate = 0.0f;   // evaporation = evap_rate * d_fs
     if (consol) {
-        evap = S.lr * P.gf_consol * (1.0f - coh) * d_fs;
+        evap_rate = S.lr * P.gf_consol * (1.0f - coh);
     } else {
-        step_live = step_live + P.weight_decay * (d_fs * scale_fwd);
+        step_live = mad_as(gpu, P.weight_decay, d_fs * scale_fwd, step_live);
     }
     // accumulation (dynamic flags only): the beta1 and evaporation terms are
     // scaled by consf (prototype_packed_b.py:661); consf == 1 changes nothing
     const bool accum = (FL & FL_DYNAMIC) && S.accum;
     const float delta_grad = -S.lr * step_live * scale_inv;
     float delta_t = accum ? delta_grad - S.consf * (P.beta1 * d_fs) : delta_grad - P.beta1 * d_fs;
-    if (consol) delta_t = accum ? delta_t - S.consf * evap : delta_t - evap;
+    if (consol) {
+        if (accum) delta_t = delta_t - S.consf * (evap_rate * d_fs);
+        else delta_t = gpu ? __fmaf_rn(-evap_rate, d_fs, delta_t) : delta_t - evap_rate * d_fs;
+    }
 
     s_fast = s_fast + sr_tick(delta_t, hash_uniform(s_fast, pos, S.salt));
 
@@ -156,15 +183,17 @@ __device__ __forceinline__ ElemOut adamw_post(const concord_step_params& P, cons
     if (F & CONCORD_F_APPLY_CHASE) {
         float chase_mantissa;
         if (F & CONCORD_F_RATIO_COH) {
-            const float gate = S.chase_floor + S.om_chase_floor * coh;
+            const float gate = gpu ? __fmaf_rn(1.0f - S.chase_floor, coh, S.chase_floor)
+                                   : S.chase_floor + S.om_chase_floor * coh;
             chase_mantissa = P.alpha * gate * P.gate_gain * (float)s_fast;
         } else if (F & CONCORD_F_COHPRE) {
-            const float gate = coh + e.cp * (1.0f - coh);
-            cp_new = P.one_minus_alpha_v_fast * e.cp + P.alpha_v_fast * coh;
+            const float gate = mad_as(gpu, e.cp, 1.0f - coh, coh);
+            cp_new = gpu ? __fmaf_rn(P.alpha_v_fast, coh, (1.0f - P.alpha_v_fast) * e.cp)
+                         : P.one_minus_alpha_v_fast * e.cp + P.alpha_v_fast * coh;
             chase_mantissa = (SAFE && (FL & FL_PLAIN)) ? P.alpha * gate * (float)s_fast   // gate_gain == 1
                                                        : P.alpha * gate * P.gate_gain * (float)s_fast;
         } else {
-            chase_mantissa = P.alpha_gate_gain * (float)s_fast;
+            chase_mantissa = (gpu ? P.alpha * P.gate_gain : P.alpha_gate_gain) * (float)s_fast;
         }
         if (accum) chase_mantissa = chase_mantissa * S.consf;   // prototype_packed_b.py:695
         const int32_t ts = sr_tick(chase_mantissa / 128.0f, hash_uniform(s_fast, pos, S.salt ^ 0x5A5A5A5A));
@@ -174,7 +203,8 @@ __device__ __forceinline__ ElemOut adamw_post(const concord_step_params& P, cons
         float delta_v8 = P.alpha_v_fast * (float)(s_slow * 128 - v_slow * 128) / 128.0f;
         if (accum) delta_v8 = delta_v8 * S.consf;                // prototype_packed_b.py:709
         if (F & CONCORD_F_RATIO_COH)
-            delta_v8 = delta_v8 * (S.leak_floor + S.om_leak_floor * coh);
+            delta_v8 = delta_v8 * (gpu ? __fmaf_rn(1.0f - S.leak_floor, coh, S.leak_floor)
+                                       : S.leak_floor + S.om_leak_floor * coh);
         const int32_t tv = sr_tick(delta_v8, hash_uniform(s_fast, pos, S.salt ^ 0x33335555));
         new_v = clampi(v_slow + tv, -128, 127);
         if (F & CONCORD_F_MASS_PRESERVE) s_slow = s_slow - (new_v - v_slow);
@@ -213,6 +243,7 @@ __device__ __forceinline__ void adamw_post_lockstep(const concord_step_params& P
                                                     const float (&step_div)[W], const StepScalars& S,
                                                     const int32_t (&pos)[W], ElemOut (&o)[W]) {
     const uint32_t F = flags_of<FL>(P);
+    const bool gpu = gpu_of<FL>(P);
     const bool plain = (FL & FL_PLAIN) != 0;
     const bool consol = (F & CONCORD_F_GF_CONSOL) != 0;
     const bool accum = (FL & FL_DYNAMIC) && S.accum;   // same gating as adamw_post
@@ -221,13 +252,16 @@ __device__ __forceinline__ void adamw_post_lockstep(const concord_step_params& P
 #pragma unroll
     for (int j = 0; j < W; ++j) {
         const float scale_fwd = pow2_exp<true>(e[j].te), scale_inv = pow2_exp<true>(-e[j].te);
-        float step_live = clamp_np(step_div[j], P.step_cap);
-        float evap = 0.0f;
-        if (consol) evap = S.lr * P.gf_consol * (1.0f - e[j].coh) * e[j].d_fs;
-        else if (!plain) step_live = step_live + P.weight_decay * (e[j].d_fs * scale_fwd);
+        float step_live = gpu ? clamp_gpu(step_div[j], -P.step_cap, P.step_cap) : clamp_np(step_div[j], P.step_cap);
+        float evap_rate = 0.0f;   // evaporation = evap_rate * d_fs
+        if (consol) evap_rate = S.lr * P.gf_consol * (1.0f - e[j].coh);
+        else if (!plain) step_live = mad_as(gpu, P.weight_decay, e[j].d_fs * scale_fwd, step_live);
         float delta_t = -S.lr * step_live * scale_inv;
         if (!plain) delta_t = accum ? delta_t - S.consf * (P.beta1 * e[j].d_fs) : delta_t - P.beta1 * e[j].d_fs;
-        if (consol) delta_t = accum ? delta_t - S.consf * evap : delta_t - evap;
+        if (consol) {
+            if (accum) delta_t = delta_t - S.consf * (evap_rate * e[j].d_fs);
+            else delta_t = gpu ? __fmaf_rn(-evap_rate, e[j].d_fs, delta_t) : delta_t - evap_rate * e[j].d_fs;
+        }
         sf[j] = e[j].s_fast + sr_tick(delta_t, hash_uniform(e[j].s_fast, pos[j], S.salt));
         ss[j] = e[j].s_slow;
         nv[j] = e[j].v_slow;
@@ -239,14 +273,16 @@ __device__ __forceinline__ void adamw_post_lockstep(const concord_step_params& P
             const float coh = e[j].coh;
             float chase_mantissa;
             if (F & CONCORD_F_RATIO_COH) {
-                const float gate = S.chase_floor + S.om_chase_floor * coh;
+                const float gate = gpu ? __fmaf_rn(1.0f - S.chase_floor, coh, S.chase_floor)
+                                       : S.chase_floor + S.om_chase_floor * coh;
                 chase_mantissa = P.alpha * gate * P.gate_gain * (float)sf[j];
             } else if (F & CONCORD_F_COHPRE) {
-                const float gate = coh + e[j].cp * (1.0f - coh);
-                cpn[j] = P.one_minus_alpha_v_fast * e[j].cp + P.alpha_v_fast * coh;
+                const float gate = mad_as(gpu, e[j].cp, 1.0f - coh, coh);
+                cpn[j] = gpu ? __fmaf_rn(P.alpha_v_fast, coh, (1.0f - P.alpha_v_fast) * e[j].cp)
+                             : P.one_minus_alpha_v_fast * e[j].cp + P.alpha_v_fast * coh;
                 chase_mantissa = plain ? P.alpha * gate * (float)sf[j] : P.alpha * gate * P.gate_gain * (float)sf[j];
             } else {
-                chase_mantissa = P.alpha_gate_gain * (float)sf[j];
+                chase_mantissa = (gpu ? P.alpha * P.gate_gain : P.alpha_gate_gain) * (float)sf[j];
             }
             if (accum) chase_mantissa = chase_mantissa * S.consf;
             const int32_t ts = sr_tick(chase_mantissa / 128.0f, hash_uniform(sf[j], pos[j], S.salt ^ 0x5A5A5A5A));
@@ -259,7 +295,8 @@ __device__ __forceinline__ void adamw_post_lockstep(const concord_step_params& P
             float delta_v8 = P.alpha_v_fast * (float)(ss[j] * 128 - v_slow * 128) / 128.0f;
             if (accum) delta_v8 = delta_v8 * S.consf;
             if (F & CONCORD_F_RATIO_COH)
-                delta_v8 = delta_v8 * (S.leak_floor + S.om_leak_floor * e[j].coh);
+                delta_v8 = delta_v8 * (gpu ? __fmaf_rn(1.0f - S.leak_floor, e[j].coh, S.leak_floor)
+                                           : S.leak_floor + S.om_leak_floor * e[j].coh);
             const int32_t tv = sr_tick(delta_v8, hash_uniform(sf[j], pos[j], S.salt ^ 0x33335555));
             nv[j] = clampi(v_slow + tv, -128, 127);
             if (F & CONCORD_F_MASS_PRESERVE) ss[j] = ss[j] - (nv[j] - v_slow);
@@ -301,8 +338,9 @@ __device__ __forceinline__ ElemOut step_adamw(const concord_step_params& P, int3
                                               float cp, const StepScalars& S, int32_t pos) {
     AdamwPre e = adamw_pre<FL>(P, packed, g, row_e, col_e, v_row, v_col, cp, S);
     fixed_coh_divide<FL>(P, e);
-    const float denom_p = crmath::cr_exp2f(P.precond_p * crmath::cr_log2f(e.x));
-    return adamw_post<FL>(P, e, e.g / denom_p, S, pos);
+    const bool gpu = gpu_of<FL>(P);
+    const float denom_p = pow2log2_as(gpu, P.precond_p, e.x);
+    return adamw_post<FL>(P, e, gpu ? div_full(e.g, denom_p) : e.g / denom_p, S, pos);
 }
 
 // Out-of-line element for rows/columns whose exponents could leave the
@@ -538,9 +576,15 @@ __global__ void __launch_bounds__(STEP_THREADS, MINB) step_vec_kernel(StepArgs A
                     }
 #pragma unroll
                     for (int u = 0; u < STEP_LOCK; ++u) fixed_coh_divide<FL>(A.P, pre[u]);
-                    crmath::cr_pow2log2<STEP_LOCK>(xs, A.P.precond_p, den);
+                    if (gpu_of<FL>(A.P)) {
 #pragma unroll
-                    for (int u = 0; u < STEP_LOCK; ++u) den[u] = pre[u].g / den[u];
+                        for (int u = 0; u < STEP_LOCK; ++u)
+                            den[u] = div_full(pre[u].g, pow2log2_as(true, A.P.precond_p, xs[u]));
+                    } else {
+                        crmath::cr_pow2log2<STEP_LOCK>(xs, A.P.precond_p, den);
+#pragma unroll
+                        for (int u = 0; u < STEP_LOCK; ++u) den[u] = pre[u].g / den[u];
+                    }
                     int32_t posv[STEP_LOCK];
 #pragma unroll
                     for (int u = 0; u < STEP_LOCK; ++u) posv[u] = posn ^ (int32_t)(k0 + h + u);
@@ -659,8 +703,13 @@ static void launch_vec(bool adamw, uint32_t F, bool has_cp, dim3 grid, cudaStrea
                          A.P.beta1 == 0.0f && A.P.v_scale == 0.0f && A.P.gf_trust_delta_sq == 1.0f &&
                          A.P.gate_gain == 1.0f && fabsf(A.P.drift_cancel_C) <= 1.0f;
     const bool runtime_scalars = A.P.consolidate != nullptr || A.P.ratio_floors != nullptr;
+    const bool gpu = A.P.arith == CONCORD_ARITH_GPU;
     if (!adamw) step_vec_kernel<CONCORD_KIND_SGD, FL_DYNAMIC, MINB><<<grid, STEP_THREADS, 0, s>>>(A);
     else if (runtime_scalars) step_vec_kernel<CONCORD_KIND_ADAMW, FL_DYNAMIC, MINB><<<grid, STEP_THREADS, 0, s>>>(A);
+    else if (F == (FL_BARE & 0xffffu) && has_cp && zero_wd && gpu)
+        step_vec_kernel<CONCORD_KIND_ADAMW, FL_BARE | FL_GPU, MINB><<<grid, STEP_THREADS, 0, s>>>(A);
+    else if (F == (FL_NOCOHPRE & 0xffffu) && zero_wd && gpu)
+        step_vec_kernel<CONCORD_KIND_ADAMW, FL_NOCOHPRE | FL_GPU, MINB><<<grid, STEP_THREADS, 0, s>>>(A);
     else if (F == (FL_BARE & 0xffffu) && has_cp && zero_wd) step_vec_kernel<CONCORD_KIND_ADAMW, FL_BARE, MINB><<<grid, STEP_THREADS, 0, s>>>(A);
     else if (F == (FL_NOCOHPRE & 0xffffu) && zero_wd) step_vec_kernel<CONCORD_KIND_ADAMW, FL_NOCOHPRE, MINB><<<grid, STEP_THREADS, 0, s>>>(A);
     else step_vec_kernel<CONCORD_KIND_ADAMW, FL_DYNAMIC, MINB><<<grid, STEP_THREADS, 0, s>>>(A);
@@ -690,6 +739,8 @@ static int step_impl(const concord_step_params* p, int32_t* packed, int64_t ldp,
     const bool need_vhat = adamw && (F & (CONCORD_F_GF_TRUST | CONCORD_F_GF_CONSOL | CONCORD_F_COHPRE | CONCORD_F_RATIO_COH));
     if (adamw && !eps) return fail(CONCORD_EINVAL, "concord_step: eps is required for adamw");
     if (p->step_cap != p->step_cap) return fail(CONCORD_EINVAL, "concord_step: step_cap is NaN");
+    if (p->arith != CONCORD_ARITH_GPU && p->arith != CONCORD_ARITH_CR)
+        return fail(CONCORD_EINVAL, "concord_step: arith must be CONCORD_ARITH_GPU or CONCORD_ARITH_CR");
     if (need_vhat && (!v_row || !v_col || !sum_v_inv))
         return fail(CONCORD_EINVAL, "concord_step: gf_trust/gf_consol/coh_pre/ratio need v_row, v_col, sum_v_inv");
     if ((F & CONCORD_F_TRACK_REBALANCE) && (!row_max || !col_max))

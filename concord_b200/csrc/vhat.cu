@@ -459,29 +459,34 @@ constexpr size_t VHAT_STATIC_SCRATCH_BYTES = 4u << 20;  // 4 MiB per device
 static __device__ __align__(256) unsigned char g_vhat_scratch[VHAT_STATIC_SCRATCH_BYTES];
 
 constexpr int MAX_DEVICES = 64;
-static void* g_vhat_scratch_ptr[MAX_DEVICES];  // device address of g_vhat_scratch, per device
+static void* g_vhat_scratch_ptr[MAX_DEVICES];  // last device address of g_vhat_scratch seen, per device
 static std::mutex g_vhat_scratch_mu;
 
-// Once per device, with that device current: look up the array's device
-// address (the host-side name is only a stand-in) and clear it.
+// Every call, with the caller's device current: look up the array's device
+// address (the host-side name is only a stand-in; the lookup is a host-side
+// table query).  The first call that sees an address for a device, or a new
+// address for it (a new CUDA context after cudaDeviceReset, or another
+// context made current on the same device), clears the array on the caller's
+// stream, because the kernels expect their counters to start at zero and
+// leave them at zero when they finish.
 static int vhat_scratch_for_current_device(void** out, cudaStream_t stream) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES)
         return fail(CONCORD_ENODEVICE, "concord_vhat_update_noalloc: no usable current CUDA device");
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_vhat_scratch);
+    if (e != cudaSuccess || !p)
+        return fail(CONCORD_ELAUNCH, std::string("concord_vhat_update_noalloc: cudaGetSymbolAddress failed: ") +
+                                         cudaGetErrorString(e));
     std::lock_guard<std::mutex> lock(g_vhat_scratch_mu);
-    if (!g_vhat_scratch_ptr[dev]) {
-        void* p = nullptr;
-        cudaError_t e = cudaGetSymbolAddress(&p, g_vhat_scratch);
-        if (e != cudaSuccess || !p)
-            return fail(CONCORD_ELAUNCH, std::string("concord_vhat_update_noalloc: cudaGetSymbolAddress failed: ") +
-                                             cudaGetErrorString(e));
+    if (g_vhat_scratch_ptr[dev] != p) {
         e = cudaMemsetAsync(p, 0, VHAT_STATIC_SCRATCH_BYTES, stream);
         if (e != cudaSuccess)
             return fail(CONCORD_ELAUNCH, std::string("concord_vhat_update_noalloc: clearing scratch failed: ") +
-                                             cudaGetErrorString(e));
+                                         cudaGetErrorString(e));
         g_vhat_scratch_ptr[dev] = p;
     }
-    *out = g_vhat_scratch_ptr[dev];
+    *out = p;
     return CONCORD_OK;
 }
 

@@ -254,8 +254,14 @@ class RowShardedStep:
     Every rank holds a full-size layer; rank r keeps rows [r0, r1) of its packed
     state current.  `step(grad_local)` takes this rank's bf16 dW partial [N, K];
     afterwards every rank holds the same bf16 forward weight, v_col and
-    sum_v_inv.  Call `rebalance()` (not the layer's) after each step, and
-    `gather_state()` before reading the full packed state.
+    sum_v_inv.  Call `gather_state()` before reading the full packed state.
+
+    Constructing it registers the layer as data-parallel: from then on the
+    layer's own autograd backward hands its local dW to `step()` (instead of
+    stepping on it), and `layer.rebalance()` runs `rebalance()` here, so a
+    model trains data-parallel through `loss.backward()` with no extra calls.
+    Calling `step()` by hand as well would step the layer a second time.
+    `close()` unregisters the layer.
     """
 
     def __init__(self, layer, group=None, kernels=None, transport=None, timeout_s=10.0):
@@ -296,6 +302,10 @@ class RowShardedStep:
             self.grad_pad = None if self.even else torch.zeros(pad, K, dtype=torch.bfloat16, device=dev)
             self.wpad = None if self.even else torch.zeros(pad, K, dtype=torch.bfloat16, device=dev)
             self.wshard = torch.zeros(self.S, K, dtype=torch.bfloat16, device=dev)
+        key = layer.packed_w.data_ptr()
+        if key in _pb._SHARDED:
+            raise RuntimeError("this layer already has a RowShardedStep; close() it first")
+        _pb._SHARDED[key] = self
 
     def check(self):
         """Raise if a cross-GPU wait of the peer transport ran out (synchronises)."""
@@ -305,7 +315,9 @@ class RowShardedStep:
 
     def close(self):
         """Collective: give the layer an ordinary forward-weight buffer back and
-        release the peer mappings."""
+        release the peer mappings.  The layer steps on its own again afterwards."""
+        if _pb._SHARDED.get(self.layer.packed_w.data_ptr()) is self:
+            del _pb._SHARDED[self.layer.packed_w.data_ptr()]
         if self.peer is not None:
             L = self.layer
             L._bf16_weight_buf = self.peer.wbuf.clone()

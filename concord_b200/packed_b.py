@@ -13,6 +13,7 @@ forward / dX / dW run through `concord_b200.gemm`.
 import ctypes
 from types import SimpleNamespace
 
+import numpy as np
 import torch
 import torch.nn as nn
 
@@ -81,18 +82,60 @@ def set_ratio_coh_floors(chase, leak):
         t[1] = _RATIO_LEAK_FLOOR
 
 
-_REB_STATS = None
+# fp32 arithmetic of the packed step: "gpu" reproduces the reference as it
+# runs compiled on NVIDIA GPUs (ex2.approx, CUDA log2f, div.full, its fma
+# contractions), "cr" the correctly rounded model that the CPU oracle restates.
+_ARITH = _abi.ARITH_GPU
+
+
+def set_arithmetic(mode):
+    """Select the step's fp32 arithmetic: "gpu" (default) or "cr".  Read at
+    every launch; a captured CUDA graph keeps the mode it was captured with."""
+    global _ARITH
+    modes = {"gpu": _abi.ARITH_GPU, "cr": _abi.ARITH_CR}
+    if mode not in modes:
+        raise ValueError(f"arithmetic must be one of {sorted(modes)}, got {mode!r}")
+    _ARITH = modes[mode]
+
+
+def get_arithmetic():
+    return "gpu" if _ARITH == _abi.ARITH_GPU else "cr"
+
+
+_REB_STATS = None      # host-side counts while instrumentation is on
+_REB_COUNTERS = {}     # device -> int64[3] counters the rebalance kernels add to
 
 
 def reset_reb_stats():
-    """Start accumulating rebalance fire counts (packed_b.py:1100-1106)."""
+    """Start (or restart) the rebalance instrumentation (packed_b.py:1100-1106).
+
+    Tick counts and clipped words are counted on the GPU by the rebalance
+    launch itself; nothing synchronises until get_reb_stats() reads them."""
     global _REB_STATS
-    _REB_STATS = dict(calls=0, tickup_dim=0, tickdown_dim=0, dim_total=0,
-                      clip_elems=0, elem_total=0)
+    _REB_STATS = dict(calls=0, dim_total=0, elem_total=0)
+    for t in _REB_COUNTERS.values():
+        t.zero_()
+
+
+def _reb_counters(device):
+    key = str(device)
+    if key not in _REB_COUNTERS:
+        _REB_COUNTERS[key] = torch.zeros(3, dtype=torch.int64, device=device)
+    return _REB_COUNTERS[key]
 
 
 def get_reb_stats():
-    return _REB_STATS
+    """The reference's rebalance statistics: calls, rows+columns ticked up and
+    down, their total, words clipped by a tick-down shift and the words seen
+    (None until reset_reb_stats())."""
+    if _REB_STATS is None:
+        return None
+    dev = [0, 0, 0]
+    for t in _REB_COUNTERS.values():
+        dev = [a + int(b) for a, b in zip(dev, t.tolist())]
+    return dict(calls=_REB_STATS["calls"], tickup_dim=dev[0], tickdown_dim=dev[1],
+                dim_total=_REB_STATS["dim_total"], clip_elems=dev[2],
+                elem_total=_REB_STATS["elem_total"])
 
 
 # ---- device scalars (packed_b.py:315-359) ----
@@ -244,7 +287,7 @@ def adamw_params(alpha=0.1, beta1=0.0, weight_decay=0.0, step_cap=10.0, v_scale=
         wd_sv=wd_sv, wd_sf=wd_sf, gf_trust_delta_sq=gf_trust_delta_sq, gate_gain=_GATE_GAIN,
         chase_floor=_RATIO_CHASE_FLOOR, leak_floor=_RATIO_LEAK_FLOOR,
         mass_preserve=mass_preserve, apply_chase=apply_chase, track_rebalance=track_rebalance,
-        use_cohpre=use_cohpre, fixed_coh=_USE_FIXED_COH, ratio_coh=_RATIO_COH)
+        use_cohpre=use_cohpre, fixed_coh=_USE_FIXED_COH, ratio_coh=_RATIO_COH, arith=_ARITH)
     if device is not None:
         key = _dev_key(device)
         if key in _CONSOLIDATE_FLAGS:
@@ -408,7 +451,8 @@ def apply_packed_sgd(packed_w, grad_W, weight_buf, row_exp, col_exp, row_max, co
     assert weight_buf.shape == packed_w.shape
     params = _abi.make_step_params(kind="sgd", mantissa_bias=mantissa_bias, alpha=alpha,
                                    beta1=beta1, alpha_v_fast=alpha_v_fast,
-                                   mass_preserve=mass_preserve, track_rebalance=track_rebalance)
+                                   mass_preserve=mass_preserve, track_rebalance=track_rebalance,
+                                   arith=_ARITH)
     salt = _get_step_counter(packed_w.device)
     if bump_salt:
         _salt_bump(salt)
@@ -449,9 +493,12 @@ def rebalance_packed(packed_w, row_exp, col_exp, row_max, col_max, MAX_M=24000, 
     _need_cuda(packed_w, row_exp, col_exp, row_max, col_max, seed_buf)
     if not bump_seed:
         seed_buf.sub_(1)   # the kernel adds it back: the launch sees the caller's value
+    stats = None
     if _REB_STATS is not None:
-        _accumulate_reb_stats(packed_w, row_exp, col_exp, row_max, col_max, MAX_M, EXP_MAX,
-                              EXP_MIN, allow_tickdown)
+        stats = _reb_counters(packed_w.device)
+        _REB_STATS["calls"] += 1
+        _REB_STATS["dim_total"] += N + K
+        _REB_STATS["elem_total"] += N * K
     lib = _lib()
     nbytes = lib.concord_rebalance_workspace_bytes(N, K)
     ws = _workspace("rebalance", nbytes, packed_w.device)
@@ -459,44 +506,35 @@ def rebalance_packed(packed_w, row_exp, col_exp, row_max, col_max, MAX_M=24000, 
         _ptr(packed_w), packed_w.stride(0), _ptr(row_exp), _ptr(col_exp), _ptr(row_max),
         _ptr(col_max), _ptr(row_hwm), _ptr(col_hwm), _ptr(seed_buf), int(MAX_M), int(EXP_MAX),
         int(EXP_MIN), int(bool(allow_tickdown)), N, K, int(row0),
-        int(N if n_total is None else n_total), _ptr(fired_out), _ptr(ws), ws.numel(),
+        int(N if n_total is None else n_total), _ptr(fired_out), _ptr(stats), _ptr(ws), ws.numel(),
         _stream(packed_w.device)), "concord_rebalance")
-
-
-@torch.no_grad()
-def _accumulate_reb_stats(packed_w, row_exp, col_exp, row_max, col_max, MAX_M, EXP_MAX, EXP_MIN,
-                          allow_tickdown):
-    """Optional instrumentation (packed_b.py:1161-1179); host-synchronising, off by default."""
-    s_slow = (packed_w << 16) >> 24
-    v_slow = (packed_w << 24) >> 24
-    i8mag = torch.maximum(s_slow.abs(), v_slow.abs())
-    re, ce = row_exp.to(torch.int32), col_exp.to(torch.int32)
-    ru = (row_max > MAX_M) & (re < EXP_MAX)
-    cu = (col_max > MAX_M) & (ce < EXP_MAX)
-    if allow_tickdown:
-        rmed = i8mag.median(dim=1).values
-        cmed = i8mag.median(dim=0).values
-        rd = (row_max <= MAX_M) & (rmed <= 31) & (re > EXP_MIN)
-        cd = (col_max <= MAX_M) & (cmed <= 31) & (ce > EXP_MIN)
-    else:
-        rd = torch.zeros_like(ru)
-        cd = torch.zeros_like(cu)
-    rt = ru.to(torch.int32) - rd.to(torch.int32)
-    ct = cu.to(torch.int32) - cd.to(torch.int32)
-    lsh = (-(rt[:, None] + ct[None, :])).clamp(min=0).to(torch.float32)
-    clip = ((i8mag.to(torch.float32) * torch.exp2(lsh)) > 127).sum().item()
-    N, K = packed_w.shape
-    _REB_STATS['calls'] += 1
-    _REB_STATS['tickup_dim'] += int(ru.sum() + cu.sum())
-    _REB_STATS['tickdown_dim'] += int(rd.sum() + cd.sum())
-    _REB_STATS['dim_total'] += N + K
-    _REB_STATS['clip_elems'] += clip
-    _REB_STATS['elem_total'] += N * K
 
 
 # ============================================================
 # Autograd Function + nn.Module (packed_b.py:1197-1856)
 # ============================================================
+
+# Data-parallel layers: packed_w.data_ptr() -> the RowShardedStep that owns the
+# layer's optimizer half (concord_b200.distributed registers it).  The
+# autograd backward and rebalance() of a registered layer go through it, so
+# `loss.backward()` trains data-parallel with no extra calls and a layer is
+# never stepped twice (once on its local dW and once sharded).
+_SHARDED = {}
+
+
+def _sharded_of(packed_w):
+    return _SHARDED.get(packed_w.data_ptr()) if _SHARDED else None
+
+
+def _optimizer_half(ctx, grad_W, step_events=None):
+    """The backward's optimizer half: this rank's row shard of the sharded
+    step when the layer is data-parallel, else the single-GPU step."""
+    dp = _sharded_of(ctx.packed_w)
+    if dp is not None:
+        dp.step(grad_W)
+    else:
+        _packed_backward_step(ctx, grad_W, step_events)
+
 
 def _packed_backward_step(ctx, grad_W, step_events=None):
     """The optimizer half of the backward (packed_b.py:1278-1337).
@@ -594,7 +632,7 @@ class FusedConcordLinearPackedB(torch.autograd.Function):
         grad_W = _gemm.grad_weight(grad_y_flat, x_flat)
         if _SIGMAG_NOISE:
             grad_W = sigmag_noise(grad_W, grad_y_flat, x_flat)
-        _packed_backward_step(ctx, grad_W)
+        _optimizer_half(ctx, grad_W)
         grad_bias = grad_y_flat.sum(0) if ctx.has_bias else None
         return (grad_x, None, None, None, grad_bias) + (None,) * 29
 
@@ -778,24 +816,36 @@ class ConcordLinearPackedB(nn.Module):
 
     @torch.no_grad()
     def get_garbage_fraction_stats(self):
-        """Quantiles of the per-weight garbage fraction noise^2 / v-hat (packed_b.py:1676-1730).
-        A host-synchronising diagnostic in torch, as in the reference."""
-        if self.v_row is None or float(self.v_row.sum().item()) <= 0.0:
+        """Summary of the per-weight garbage fraction noise^2 / v-hat in [0, 1]
+        (packed_b.py:1676-1730): mean, quartiles and the fractions below 0.1
+        and above 0.9; None before the first v-hat update.  One pass of the
+        garbage-fraction kernel; the quartiles sort its output on the GPU."""
+        if self.v_row is None:
             return None
-        s_fast = (self.packed_w >> 16).to(torch.float32)
-        s_slow = ((self.packed_w << 16) >> 24).to(torch.float32)
-        v_slow = ((self.packed_w << 24) >> 24).to(torch.float32)
-        noise = s_fast - float(self.drift_cancel_C) * (s_slow * S_SLOW_FACTOR - v_slow * V_SLOW_FACTOR)
-        exp = (self.row_exp[:, None].to(torch.float32) + self.col_exp[None, :].to(torch.float32)
-               - self.MANTISSA_BIAS)
-        var_W = (noise * torch.pow(2.0, exp)) ** 2
-        sum_v = self.v_row.float().sum().clamp(min=1e-30)
-        v_hat = self.v_row.float()[:, None] * self.v_col.float()[None, :] / sum_v
-        flat = (var_W / (v_hat + 1e-30)).clamp(0.0, 1.0).flatten()
-        q = torch.quantile(flat, torch.tensor([0.25, 0.5, 0.75], device=flat.device))
-        return {'mean': flat.mean().item(), 'p25': q[0].item(), 'median': q[1].item(),
-                'p75': q[2].item(), 'frac_signal_dominated': (flat < 0.1).float().mean().item(),
-                'frac_noise_dominated': (flat > 0.9).float().mean().item()}
+        sum_v = self.v_row.float().sum().reshape(1)
+        if float(sum_v.item()) <= 0.0:
+            return None
+        sum_v.clamp_(min=1e-30)
+        N, K = self.packed_w.shape
+        gf = torch.empty(N * K, dtype=torch.float32, device=self.packed_w.device)
+        acc = torch.zeros(3, dtype=torch.float64, device=self.packed_w.device)
+        _abi.check(_lib().concord_garbage_fraction(
+            _ptr(self.packed_w), self.packed_w.stride(0), _ptr(self.row_exp), _ptr(self.col_exp),
+            _ptr(self.v_row), _ptr(self.v_col), _ptr(sum_v), N, K, int(self.MANTISSA_BIAS),
+            float(self.drift_cancel_C), _ptr(gf), _ptr(acc), _stream(self.packed_w.device)),
+            "concord_garbage_fraction")
+        srt = torch.sort(gf).values
+        qs = []
+        for q in (0.25, 0.5, 0.75):   # linear interpolation between order statistics
+            pos = q * (N * K - 1)
+            lo = int(pos)
+            hi = min(lo + 1, N * K - 1)
+            qs.append((srt[lo], srt[hi], pos - lo))
+        qv = torch.stack([a + (b - a) * f for a, b, f in qs]).tolist()
+        tot, lo_n, hi_n = acc.tolist()
+        cnt = float(N * K)
+        return {'mean': tot / cnt, 'p25': qv[0], 'median': qv[1], 'p75': qv[2],
+                'frac_signal_dominated': lo_n / cnt, 'frac_noise_dominated': hi_n / cnt}
 
     def _ensure_buffers(self):
         N, K = self.packed_w.shape
@@ -853,12 +903,16 @@ class ConcordLinearPackedB(nn.Module):
         vals = (self.packed_w, self.row_exp, self.col_exp) + self._apply_args(wbuf, rmbuf, cmbuf)[:-1]
         ctx = SimpleNamespace(**dict(zip(_CTX_FIELDS, vals)))
         ctx.coh_stats = coh_stats if coh_stats is not None else self.coh_stats
-        _packed_backward_step(ctx, grad_W.contiguous(), step_events)
+        _optimizer_half(ctx, grad_W.contiguous(), step_events)
 
     @torch.no_grad()
     def rebalance(self, fired_out=None):
         """Tick-up rebalance from the last step's row/col max; folds the
         high-watermarks and bumps the seed on the device (packed_b.py:1792-1814)."""
+        dp = _sharded_of(self.packed_w)
+        if dp is not None:
+            dp.rebalance(fired_out)
+            return
         rmbuf = getattr(self, '_row_max_buf', None)
         cmbuf = getattr(self, '_col_max_buf', None)
         if rmbuf is None or cmbuf is None:
@@ -927,7 +981,7 @@ class FusedConcordConv2dPackedB(torch.autograd.Function):
             grad_W = torch.nn.grad.conv2d_weight(x_bf16, (out_c, in_c, kh, kw), grad_y,
                                                  stride=stride, padding=padding)
             grad_W = grad_W.reshape(out_c, -1).to(torch.bfloat16).contiguous()
-        _packed_backward_step(ctx, grad_W)
+        _optimizer_half(ctx, grad_W)
         grad_bias = grad_y.sum(dim=(0, 2, 3)) if ctx.has_bias else None
         return (grad_x, None, None, None, grad_bias) + (None,) * 35
 
@@ -997,53 +1051,77 @@ def measure_coherence(layer):
 
 
 class DissipationAutoTuner:
-    """Probe-then-commit autotuning of gf_consol (kappa) and beta1 (packed_b.py:2109-2225).
+    """Probe-then-commit choice of the evaporation rate kappa (`gf_consol`) and
+    of beta1 (packed_b.py:2109-2225).
 
-    Identical schedule and table semantics to the reference.  `meter` (default
-    `measure_coherence`) maps a layer to its mean coherence.
+    Schedule: from construction until `probe_end` every layer runs at
+    `probe_kappa` with beta1 = 0.  Every `measure_every` steps inside
+    [probe_start, probe_end) the mean gate coherence of the layers (`meter`,
+    default `measure_coherence`) is recorded.  At `probe_end` the window mean
+    picks kappa by piecewise-linear interpolation in `table` (pairs
+    (coherence, kappa) with coherence strictly descending; flat beyond either
+    end), and beta1 = `beta1_on` when that mean reaches
+    `beta1_coh_threshold`.  With `peak_lr`, the table's kappas and
+    `probe_kappa` are friction values F = lr * kappa and are divided by it.
     """
 
     def __init__(self, layers, probe_start, probe_end, table, probe_kappa=50.0,
                  measure_every=10, verbose=True, beta1_on=0.1, beta1_coh_threshold=0.35,
                  peak_lr=None, meter=None):
-        assert probe_end > probe_start >= 0
-        assert all(c1 > c2 for (c1, _), (c2, _) in zip(table, table[1:])), \
-            "table coh values must be strictly descending"
+        coh = np.asarray([float(c) for c, _ in table], dtype=np.float64)
+        kap = np.asarray([float(k) for _, k in table], dtype=np.float64)
+        if not 0 <= probe_start < probe_end:
+            raise AssertionError(f"need 0 <= probe_start < probe_end, got {probe_start}, {probe_end}")
+        if coh.size == 0 or np.any(np.diff(coh) >= 0):
+            raise AssertionError("the table's coherence column must be strictly descending")
+        unit = 1.0 if peak_lr is None else 1.0 / float(peak_lr)
+        # np.interp wants ascending abscissae: keep the table reversed
+        self._coh_up, self._kappa_up = coh[::-1].copy(), kap[::-1] * unit
+        self.table = [(float(c), float(k)) for c, k in zip(coh, kap * unit)]
         self.layers = list(layers)
         self.probe_start, self.probe_end = int(probe_start), int(probe_end)
-        self.table = [(float(c), float(k)) for c, k in table]
-        self.probe_kappa = float(probe_kappa)
+        self.probe_kappa = float(probe_kappa) * unit
         self.measure_every = max(1, int(measure_every))
         self.verbose = verbose
         self.beta1_on = float(beta1_on)
         self.beta1_coh_threshold = float(beta1_coh_threshold)
-        self.meter = meter if meter is not None else measure_coherence
-        if peak_lr is not None:
-            conv = 1.0 / float(peak_lr)
-            self.table = [(c, k * conv) for c, k in self.table]
-            self.probe_kappa = self.probe_kappa * conv
+        self.meter = measure_coherence if meter is None else meter
         self._samples = []
         self.committed = None
         self.committed_beta1 = None
-        for m in self.layers:
-            m.gf_consol = self.probe_kappa
-            m.beta1 = 0.0
+        self._set_all(self.probe_kappa, 0.0)
+
+    def _set_all(self, kappa, beta1):
+        for layer in self.layers:
+            layer.gf_consol = kappa
+            layer.beta1 = beta1
 
     def kappa_from_coh(self, c):
-        t = self.table
-        if c >= t[0][0]:
-            return t[0][1]
-        if c <= t[-1][0]:
-            return t[-1][1]
-        for (c1, k1), (c2, k2) in zip(t, t[1:]):
-            if c2 <= c <= c1:
-                return k1 + (c1 - c) / (c1 - c2) * (k2 - k1)
-        return t[-1][1]
+        """kappa for a window-mean coherence c (linear between table rows)."""
+        return float(np.interp(float(c), self._coh_up, self._kappa_up))
+
+    def _probing(self, t):
+        return self.probe_start <= t < self.probe_end and (t - self.probe_start) % self.measure_every == 0
 
     def step(self, t):
-        """Call once per step before its backward; returns kappa once, at t == probe_end."""
+        """Call at every step t before its backward.  Returns the committed kappa
+        at the step that commits it (t >= probe_end, once), otherwise None."""
         if self.committed is not None:
             return None
+        if self._probing(t) and self.layers:
+            self._samples.append(float(np.mean([self.meter(m) for m in self.layers])))
+        if t < self.probe_end:
+            return None
+        window = float(np.mean(self._samples)) if self._samples else self.table[0][0]
+        self.committed = self.kappa_from_coh(window)
+        use_b1 = self.beta1_on > 0 and window >= self.beta1_coh_threshold
+        self.committed_beta1 = self.beta1_on if use_b1 else 0.0
+        self._set_all(self.committed, self.committed_beta1)
+        if self.verbose:
+            print(f"[concord_b200] autotuner committed kappa={self.committed:g}, "
+                  f"beta1={self.committed_beta1:g} from mean coherence {window:.4f} "
+                  f"over {len(self._samples)} probes in steps [{self.probe_start}, {self.probe_end})")
+        return self.committed
         if self.probe_start <= t < self.probe_end and (t - self.probe_start) % self.measure_every == 0:
             vals = [self.meter(m) for m in self.layers]
             if vals:

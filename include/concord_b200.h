@@ -37,6 +37,7 @@
  *                            consolidated_weight (1632-1649)
  *   concord_quantize      <- ConcordLinearPackedB.load_weights (1570-1603),
  *                            load_weights_finetune (1816-1856)
+ *   concord_garbage_fraction <- get_garbage_fraction_stats (packed_b.py:1676-1730)
  *   concord_coherence     <- measure_coherence / gate_coherence_from_fields
  *                            (packed_b.py:2081-2106)
  *   concord_gemm_fwd/dx/dw <- F.linear / grad_y @ W / grad_y^T @ x
@@ -59,7 +60,7 @@
 extern "C" {
 #endif
 
-#define CONCORD_ABI_VERSION 2
+#define CONCORD_ABI_VERSION 3
 
 /* status codes */
 #define CONCORD_OK            0
@@ -84,6 +85,23 @@ extern "C" {
 
 #define CONCORD_KIND_ADAMW 0
 #define CONCORD_KIND_SGD   1
+
+/*
+ * fp32 arithmetic of the step (concord_step_params.arith).
+ *   CONCORD_ARITH_GPU (default): the reference's kernel as compiled by Triton
+ *     for NVIDIA GPUs: tl.exp2 = ex2.approx.f32, tl.log2 = CUDA log2f, `/` =
+ *     div.full.f32, min/max drop NaN, and multiply-add contracted to fma where
+ *     the compiled reference contracts it.  Scalars the kernel combines
+ *     (1 - alpha_v_fast, 1 - floors, alpha * gate_gain) are combined in fp32
+ *     in the kernel, as the compiled reference does.  Words bit-identical to
+ *     the reference running on a B200.
+ *   CONCORD_ARITH_CR: every fp32 operation rounded once, exp2/log2 correctly
+ *     rounded, IEEE division, numpy NaN semantics: the model the CPU oracle
+ *     restates (and the reference under its CPU interpreter with correctly
+ *     rounded exp2/log2); the one_minus_* / alpha_gate_gain fields are used.
+ */
+#define CONCORD_ARITH_GPU 0
+#define CONCORD_ARITH_CR  1
 
 /*
  * Launch-time scalars of one packed step.  Every float is the fp32 value
@@ -132,6 +150,7 @@ typedef struct concord_step_params {
      */
     const int32_t* consolidate;
     const float* ratio_floors;
+    int32_t arith;                  /* CONCORD_ARITH_GPU (0) or CONCORD_ARITH_CR (1) */
 } concord_step_params;
 
 int         concord_abi_version(void);
@@ -166,9 +185,11 @@ int concord_vhat_update(const uint16_t* grad, int64_t ldg, int64_t N, int64_t K,
  * (concord_vhat_noalloc_max_scratch_bytes()), held by every GPU that loads
  * the library until the process exits.  Sizes whose
  * concord_vhat_workspace_bytes(N, K) exceed it are rejected with
- * CONCORD_ETOOBIG.  The first call on a device, with that device current,
- * looks up the array's device address and clears it on `stream`; make that
- * first call before any stream capture.  All calls on a device share the one
+ * CONCORD_ETOOBIG.  Every call looks up the array's device address for the
+ * current device (a host-side query); the first call on a device, and the
+ * first call after that address changes (a new CUDA context on the device,
+ * e.g. after cudaDeviceReset), clears the array on `stream`: make that first
+ * call before any stream capture.  All calls on a device share the one
  * array: calls that may overlap on the GPU (different streams without
  * ordering) race and must be serialised by the caller.  Nothing else differs
  * from concord_vhat_update: same results, bit for bit.
@@ -368,8 +389,13 @@ int concord_peer_allreduce(const void* in, void* out, int64_t count, int32_t op,
  * left-shifts where a tick-down fires (allow_tickdown only).  N_total is
  * the global row count and row0 the first global row (Philox offsets use
  * global indices).  fired_out (nullable, device int32) is set to 1 when any
- * exponent moved, else 0.  Workspace: concord_rebalance_workspace_bytes(N, K),
- * zero-filled before first use.
+ * exponent moved, else 0.  stats (nullable, device uint64[3]) accumulates
+ * the reference's optional rebalance instrumentation (packed_b.py:1161-1179):
+ * [0] += rows+columns ticked up, [1] += rows+columns ticked down, [2] += words
+ * whose larger int8 field exceeds 127 once the tick-down left shift is
+ * applied (one extra read pass over the words, only when stats != NULL).
+ * Workspace: concord_rebalance_workspace_bytes(N, K), zero-filled before
+ * first use.
  */
 size_t concord_rebalance_workspace_bytes(int64_t N, int64_t K);
 int concord_rebalance(int32_t* packed, int64_t ldp,
@@ -379,7 +405,7 @@ int concord_rebalance(int32_t* packed, int64_t ldp,
                       int32_t* seed, int32_t max_m, int32_t exp_max, int32_t exp_min,
                       int32_t allow_tickdown,
                       int64_t N, int64_t K, int64_t row0, int64_t N_total,
-                      int32_t* fired_out,
+                      int32_t* fired_out, unsigned long long* stats,
                       void* workspace, size_t workspace_bytes, void* stream);
 
 /* bf16 weight = (m_eff or the slow part only) * 2^(row_exp+col_exp-bias), RNE. */
@@ -405,6 +431,19 @@ int concord_quantize(const float* W, int64_t ldw, int32_t* packed, int64_t ldp,
  */
 int concord_coherence(const int32_t* packed, int64_t ldp, int64_t N, int64_t K,
                       float drift_cancel_C, double* out, void* stream);
+
+/*
+ * Garbage-fraction diagnostic of the packed state
+ * (ConcordLinearPackedB.get_garbage_fraction_stats, packed_b.py:1676-1730):
+ * gf = clamp((noise * 2^(row_exp+col_exp-bias))^2 / (v_hat + 1e-30), 0, 1),
+ * noise = s_fast - C * 128 * (s_slow - v_slow), v_hat = v_row v_col / *sum_v.
+ * gf_out (nullable, contiguous [N,K] fp32) receives gf; acc (device double[3],
+ * zeroed by the caller) += sum of gf, count of gf < 0.1, count of gf > 0.9.
+ */
+int concord_garbage_fraction(const int32_t* packed, int64_t ldp, const int8_t* row_exp,
+                             const int8_t* col_exp, const float* v_row, const float* v_col,
+                             const float* sum_v, int64_t N, int64_t K, int32_t mantissa_bias,
+                             float drift_cancel_C, float* gf_out, double* acc, void* stream);
 
 /*
  * The layer's dense GEMMs on the tensor cores (tcgen05/TMEM, TMA-fed), bf16

@@ -17,3 +17,13 @@ def oracle_mod():
     from oracle import oracle
     oracle.lib()
     return oracle
+
+
+@pytest.fixture(autouse=True)
+def cr_arithmetic_by_default():
+    """Tests compare against the CPU oracle, which restates the correctly
+    rounded model; a test of the reference-GPU arithmetic selects "gpu" itself."""
+    from concord_b200 import packed_b
+    packed_b.set_arithmetic("cr")
+    yield
+    packed_b.set_arithmetic("gpu")

@@ -3,7 +3,7 @@ import os
 
 import numpy as np
 
-from concord_b200._abi import make_step_params
+from concord_b200._abi import ARITH_CR, make_step_params
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 STEP_CASES = ["bare", "nocohpre", "consol", "ratio", "legacycoh", "wd_beta1", "nochase",
@@ -15,14 +15,15 @@ def load(name):
 
 
 def params_of(z):
-    """StepParams for a fixture, built by the same host rule the package uses."""
+    """StepParams for a fixture, built by the same host rule the package uses.
+    The interpreter fixtures record the correctly rounded model (ARITH_CR)."""
     f = lambda k, d=0.0: float(z["cfg_" + k]) if ("cfg_" + k) in z else d  # noqa: E731
     b = lambda k: bool(z["cfg_" + k])  # noqa: E731
     kind = str(z["cfg_kind"])
     if kind == "sgd":
         return make_step_params(kind="sgd", alpha=f("alpha"), beta1=f("beta1"),
                                 alpha_v_fast=f("alpha_v_fast"), mass_preserve=b("mass_preserve"),
-                                track_rebalance=b("track_rebalance"))
+                                track_rebalance=b("track_rebalance"), arith=ARITH_CR)
     return make_step_params(
         kind="adamw", alpha=f("alpha"), beta1=f("beta1"), weight_decay=f("weight_decay"),
         step_cap=f("step_cap"), v_scale=f("v_scale"), precond_p=f("precond_p"),
@@ -32,7 +33,7 @@ def params_of(z):
         chase_floor=f("chase_floor"), leak_floor=f("leak_floor"),
         mass_preserve=b("mass_preserve"), apply_chase=b("apply_chase"),
         track_rebalance=b("track_rebalance"), use_cohpre=b("cohpre"),
-        fixed_coh=b("fixed_coh"), ratio_coh=b("ratio"))
+        fixed_coh=b("fixed_coh"), ratio_coh=b("ratio"), arith=ARITH_CR)
 
 
 def lr_eps(z):

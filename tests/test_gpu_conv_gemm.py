@@ -125,9 +125,9 @@ def test_cudnn_backend_switch():
         calls.append(1)
         return orig_bwd(*a)
 
-    def spy_step(ctx, grad_W):
+    def spy_step(ctx, grad_W, *rest):
         dws.append(grad_W.float().clone())
-        return orig_step(ctx, grad_W)
+        return orig_step(ctx, grad_W, *rest)
     gemm.conv2d_backward, pb._packed_backward_step = spy_bwd, spy_step
     try:
         for backend in ("cudnn", "gemm"):

@@ -32,7 +32,7 @@ def test_library_exports_header_symbols(built):
     assert declared == exported
     assert declared == set(_abi.EXPORTED)
     _abi.load()
-    assert _abi.load().concord_abi_version() == 2
+    assert _abi.load().concord_abi_version() == _abi.ABI_VERSION == 3
 
 
 def test_gemm_dw_split_decision(built):
@@ -173,3 +173,23 @@ def test_autotuner_parity():
     assert abs(fu.probe_kappa - 50.0) < 1e-9 and abs(fu.table[3][1] - 400.0) < 1e-9
     assert tuner.kappa_from_coh(0.50) == 0.0 and tuner.kappa_from_coh(0.20) == 400.0
     assert 100.0 < tuner.kappa_from_coh(0.301) < 200.0
+
+
+def test_autotuner_table_interpolation():
+    """kappa_from_coh is the table's piecewise-linear interpolant, flat beyond
+    its ends; peak_lr turns F = lr * kappa units into kappa."""
+    from concord_b200 import DissipationAutoTuner
+    TABLE = [(0.387, 0.0), (0.314, 100.0), (0.288, 200.0), (0.274, 400.0), (0.256, 400.0)]
+    tu = DissipationAutoTuner([], 0, 1, TABLE, verbose=False)
+    assert tu.kappa_from_coh(0.5) == 0.0 and tu.kappa_from_coh(0.1) == 400.0
+    for (c1, k1), (c2, k2) in zip(TABLE, TABLE[1:]):
+        for f in (0.0, 0.25, 0.5, 1.0):
+            c = c1 + f * (c2 - c1)
+            assert abs(tu.kappa_from_coh(c) - (k1 + f * (k2 - k1))) < 1e-9
+    tu = DissipationAutoTuner([], 0, 1, TABLE, probe_kappa=0.5, verbose=False, peak_lr=1e-3)
+    assert abs(tu.probe_kappa - 500.0) < 1e-9
+    assert abs(tu.kappa_from_coh(0.301) - 150.0 * 1e3) < 1e-6
+    with pytest.raises(AssertionError):
+        DissipationAutoTuner([], 0, 1, TABLE[::-1], verbose=False)
+    with pytest.raises(AssertionError):
+        DissipationAutoTuner([], 5, 5, TABLE, verbose=False)

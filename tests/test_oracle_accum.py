@@ -5,7 +5,7 @@ import numpy as np
 
 
 def _case(oracle_mod, cons):
-    from concord_b200._abi import make_step_params
+    from concord_b200._abi import ARITH_CR, make_step_params
     rng = np.random.default_rng(7)
     N, K = 24, 40
     sf = rng.integers(-3000, 3001, (N, K))
@@ -13,7 +13,7 @@ def _case(oracle_mod, cons):
     vs = rng.integers(-100, 101, (N, K))
     packed = (((sf & 0xFFFF) << 16) | ((ss & 0xFF) << 8) | (vs & 0xFF)).astype(np.uint32).view(np.int32)
     grad = oracle_mod.f32_to_bf16(rng.normal(0, 1e-2, (N, K)).astype(np.float32))
-    P = make_step_params(kind="adamw", v_scale=0.0, precond_p=0.5, drift_cancel_C=0.018,
+    P = make_step_params(kind="adamw", arith=ARITH_CR, v_scale=0.0, precond_p=0.5, drift_cancel_C=0.018,
                          gf_trust_delta_sq=1.0, gf_consol=30.0, beta1=0.3, wd_sv=0.1, wd_sf=0.05,
                          mass_preserve=True, use_cohpre=True)
     flag = np.array([0 if cons is None else cons], np.int32)

@@ -82,9 +82,9 @@ def test_layer_trajectory(oracle_mod):
     """Bare layer, 4 steps: words bit-exact given the reference's v-hat, and the
     oracle's fixed-order v-hat within fp32 summation-order tolerance."""
     z = load("layer_bare")
-    from concord_b200._abi import make_step_params
+    from concord_b200._abi import ARITH_CR, make_step_params
     from concord_b200.packed_b import compute_drift_cancel_C
-    P = make_step_params(kind="adamw", alpha=0.1, v_scale=0.0, precond_p=0.5, step_cap=10.0,
+    P = make_step_params(kind="adamw", arith=ARITH_CR, alpha=0.1, v_scale=0.0, precond_p=0.5, step_cap=10.0,
                          drift_cancel_C=compute_drift_cancel_C(0.1, 0.001, mass_preserve=True),
                          alpha_v_fast=0.001, gf_trust_delta_sq=1.0, mass_preserve=True,
                          use_cohpre=True)
