@@ -133,6 +133,32 @@ def make_grads(n_rows, k_cols, device, count=2, seed=1):
     return grads, gemm_ms
 
 
+def backward_time(n_rows, k_cols, device, iters=20):
+    """The whole layer backward through the drop-in API: `layer(x)` then
+    `y.backward(dY)` (dX and dW GEMMs, v-hat, packed step) and `rebalance()`,
+    timed with CUDA events on the stream autograd runs on (the forward is
+    outside the timed region).  Host launch gaps inside the backward count."""
+    layer = setup_layer(n_rows, k_cols, device, seed=3)
+    g = torch.Generator(device=device).manual_seed(7)
+    x = torch.randn(M, k_cols, generator=g, device=device).to(torch.bfloat16).requires_grad_(True)
+    dY = (torch.randn(M, n_rows, generator=g, device=device) / M).to(torch.bfloat16)
+    ts, fs = [], []
+    for i in range(iters + 3):
+        f0, f1, b1 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        f0.record()
+        y = layer(x)
+        f1.record()
+        y.backward(dY)
+        layer.rebalance()
+        b1.record()
+        torch.cuda.synchronize()
+        if i >= 3:
+            ts.append(f1.elapsed_time(b1))
+            fs.append(f0.elapsed_time(f1))
+    x.grad = None
+    return statistics.mean(ts), statistics.mean(fs)
+
+
 SHARDED = None
 STEP_TRAFFIC_PER_PARAM = (84.079872e6 + 53.77408e6) / (4096 * 2048)
 
@@ -363,6 +389,128 @@ def cpu_baseline(rows=2048, threads=1, reps=1):
     return bytes_ / dt / 1e9, dt
 
 
+def ref_cpu_rule(rows, threads, steps=2):
+    """Time the reference's own CPU update rule, ConcordRef.step
+    (experiments/cpu_dynamics/concord_ref.py:107-156, installed unmodified under
+    baseline/_ref), on `rows` x K of the workload with `threads` torch threads.
+    Bare mapping: gate, noise and evaporation off, lr constant.  Returns
+    (GB/s in this bench's algorithmic bytes per parameter, s/step), or None when
+    the reference is not installed."""
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "experiments")):
+        return None
+    if ref not in sys.path:
+        sys.path.append(ref)
+    from experiments.cpu_dynamics.concord_ref import ConcordRef
+    old = torch.get_num_threads()
+    torch.set_num_threads(threads)
+    try:
+        g = torch.Generator().manual_seed(0)
+        lin = torch.nn.Linear(K, rows, bias=False)
+        with torch.no_grad():
+            lin.weight.copy_(torch.randn(rows, K, generator=g) * 0.02)
+        lin.weight.grad = (torch.randn(rows, K, generator=g) * 1e-3).to(torch.bfloat16).float()
+        opt = ConcordRef(lin, lr=5e-4, total_steps=1000, warmup=0, gate=False, noise=False, kappa=0.0,
+                         lr_min_frac=1.0)
+        opt.step()                                   # warm-up
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            opt.step()
+        dt = (time.perf_counter() - t0) / steps
+    finally:
+        torch.set_num_threads(old)
+    return rows * K * (STEP_BYTES_PER_PARAM + VHAT_BYTES_PER_PARAM) / dt / 1e9, dt
+
+
+def chargpt_cpu_baseline(threads, steps=3, batch=64):
+    """BASELINE config 3's model on the host CPU with the reference's CPU
+    optimizer (ConcordRef on the Linears, its SGD-momentum on the rest), fp32:
+    steps/s on `threads` torch threads, or None without the reference."""
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "experiments")):
+        return None
+    if ref not in sys.path:
+        sys.path.append(ref)
+    from experiments.cpu_dynamics.concord_ref import ConcordRef
+    import workloads
+    old = torch.get_num_threads()
+    torch.set_num_threads(threads)
+    try:
+        torch.manual_seed(0)
+        data = workloads.MarkovChars(n_chains=256, length=600, device="cpu")
+        model = workloads.CharGPT()
+        opt = ConcordRef(model, lr=5e-4, total_steps=2000, warmup=100, gate=False, noise=False, kappa=0.0)
+        times = []
+        for it in range(steps + 1):
+            x, y = data.batch(batch, 256)
+            t0 = time.perf_counter()
+            loss = model(x, y)
+            loss.backward()
+            opt.step()
+            opt.zero_grad()
+            if it:
+                times.append(time.perf_counter() - t0)
+    finally:
+        torch.set_num_threads(old)
+    return 1.0 / statistics.mean(times)
+
+
+def bench_chargpt(args, cores):
+    """Config 3 end to end on one GPU: steps/s over the run, loss curve."""
+    import workloads
+    steps = args.steps
+    torch.cuda.reset_peak_memory_stats()
+    r = workloads.train_chargpt(steps=steps)
+    d = {"metric": "char-GPT (config 3) train steps/s", "unit": "steps/s", "n_gpus": 1, "steps": steps,
+         "warmup": 10, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+         "dtype": "bf16 autocast; packed int32 words", "data": "synthetic: order-2 Markov chain, 65 symbols, "
+         "Dirichlet(0.3) rows, seed 0", "config": {"workload": "config 3: 6L/6H/384d char-GPT, ctx 256, batch 64, "
+         "Concord on all Linears, SGD(0.9) on embeddings/norms, lr 5e-4", "seq_len": 256, "global_batch": 64},
+         "value": r["steps_per_s"], "ms_per_step": 1e3 / r["steps_per_s"],
+         "tokens_per_s": r["steps_per_s"] * r["tokens_per_step"], "losses": r["losses"],
+         "entropy_floor_nats": r["entropy_floor"], "concord_params": r["concord_params"],
+         "aux_params": r["aux_params"], "peak_mem_gb": torch.cuda.max_memory_allocated() / 1e9,
+         "timing": "host wall clock around each step with a device synchronize on both sides, steps 10.."}
+    if not args.no_cpu_baseline:
+        v1 = chargpt_cpu_baseline(1, steps=1)
+        if v1 is not None:
+            d["cpu_baseline"] = {"value": v1, "unit": "steps/s", "cores": 1, "kind": "reference",
+                                 "sample": "the same model in fp32 on the host with ConcordRef.step (2-D weights), 1 step"}
+            d["cpu_baseline_all_cores"] = {"value": chargpt_cpu_baseline(cores, steps=2), "unit": "steps/s",
+                                           "cores": cores, "kind": "reference", "sample": "same, all threads, 2 steps"}
+    emit(d)
+
+
+def bench_llama(args, rank, world):
+    """Config 5: weak-scaling data-parallel training step (whole job tokens/s)."""
+    import workloads
+    torch.cuda.reset_peak_memory_stats()
+    r = workloads.train_llama_dp(steps=args.steps, warmup=args.warmup, batch_per_gpu=args.batch,
+                                 n_layer=args.layers)
+    ms = statistics.mean(r["ms"])
+    mem = torch.tensor([torch.cuda.max_memory_allocated() / 1e9], device="cuda")
+    if world > 1:
+        dist.all_reduce(mem, op=dist.ReduceOp.MAX)
+    if rank != 0:
+        return
+    emit({"metric": "Llama-style decoder (config 5) data-parallel train tokens/s", "unit": "tokens/s",
+          "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+          "scaling": "weak", "vs_baseline": None, "dtype": "bf16 autocast; packed int32 words",
+          "data": "synthetic: uniform random token ids, vocab 32000",
+          "config": {"workload": f"config 5: {args.layers}-layer d=2048 16-head SwiGLU-5504 decoder, seq 2048, "
+                                 f"{args.batch} sequences per GPU (global batch {args.batch * world})",
+                     "seq_len": 2048, "global_batch": args.batch * world,
+                     "parallelism": f"dp{world}: row-sharded packed step per layer inside loss.backward()"},
+          "value": r["tokens_per_step"] / (ms * 1e-3), "ms_per_step": ms,
+          "ms_per_step_all": r["ms"], "loss_first_last": [r["losses"][0], r["losses"][-1]],
+          "concord_params": r["concord_params"], "peak_mem_gb_max_rank": float(mem.item()),
+          "timing": "CUDA events around forward+backward+aux step+rebalance, barrier before, max over ranks"})
+
+
+def ms_share(part, whole):
+    return part / whole if whole > 0 else None
+
+
 def emit(d):
     print(json.dumps(d), flush=True)
 
@@ -393,6 +541,12 @@ def main():
     ap.add_argument("--rows", type=int, default=N)
     ap.add_argument("--cols", type=int, default=K)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=8, help="llama: sequences per GPU")
+    ap.add_argument("--layers", type=int, default=24, help="llama: decoder layers")
+    ap.add_argument("--workload", default="c2", choices=["c2", "chargpt", "llama"],
+                    help="c2: the packed-step path on config 2's largest layer (default); "
+                         "chargpt: config 3's char-level GPT trained end to end; "
+                         "llama: config 5's data-parallel decoder (weak scaling)")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="time eager launches instead of CUDA-graph replays")
     args = ap.parse_args()
@@ -404,27 +558,45 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        # the reference path is Python+Triton with no CPU build; its CPU
-        # implementation is the oracle port, run on every host core
-        # size each step's sample so the whole run stays near one minute
-        _, t64 = cpu_baseline(rows=max(64, cores), threads=cores)
-        per_row = t64 / max(64, cores)
-        rows = int(min(4096, max(cores, 60.0 / max(1, args.steps + args.warmup) / per_row)))
-        for _ in range(args.warmup):
-            cpu_baseline(rows=rows, threads=cores)
-        vals = [cpu_baseline(rows=rows, threads=cores)[0] for _ in range(args.steps)]
+        # the reference's CPU implementation of the path: its real-valued update
+        # rule ConcordRef (the Triton step has no CPU build), on every host
+        # core; the oracle port stands in only when the reference is absent
+        probe = ref_cpu_rule(rows=256, threads=cores, steps=1)
+        if probe is not None:
+            per_row = probe[1] / 256
+            rows = int(min(args.rows, max(256, 20.0 / max(1, args.steps + args.warmup) / per_row)))
+            ref_cpu_rule(rows=rows, threads=cores, steps=max(1, args.warmup))
+            vals = [ref_cpu_rule(rows=rows, threads=cores, steps=1)[0] for _ in range(args.steps)]
+            kind, what = "reference", "ConcordRef.step (experiments/cpu_dynamics/concord_ref.py), torch CPU"
+        else:
+            _, t64 = cpu_baseline(rows=max(64, cores), threads=cores)
+            per_row = t64 / max(64, cores)
+            rows = int(min(4096, max(cores, 60.0 / max(1, args.steps + args.warmup) / per_row)))
+            for _ in range(args.warmup):
+                cpu_baseline(rows=rows, threads=cores)
+            vals = [cpu_baseline(rows=rows, threads=cores)[0] for _ in range(args.steps)]
+            kind, what = "port", "oracle port (C restatement)"
         v = statistics.mean(vals)
         d = base_line(args, 1)
         d.update({"impl": "reference", "value": v, "ms_per_step": rows * K * 22 / v / 1e6,
-                  "cpu_baseline": {"value": v, "unit": "GB/s", "cores": cores, "kind": "port",
-                                   "sample": f"{rows} rows x {K} cols of the workload per step"},
+                  "cpu_baseline": {"value": v, "unit": "GB/s", "cores": cores, "kind": kind,
+                                   "sample": f"{rows} rows x {K} cols of the workload per step; {what}"},
                   "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
         emit(d)
+        return
+    if args.workload == "chargpt":
+        if rank == 0:
+            bench_chargpt(args, cores)
         return
     if world > 1:
         torch.cuda.set_device(local)
         dist.init_process_group("nccl")
     device = torch.device("cuda", torch.cuda.current_device())
+    if args.workload == "llama":
+        bench_llama(args, rank, world)
+        if world > 1:
+            dist.destroy_process_group()
+        return
     from concord_b200 import packed_b
     packed_b._lib()
     r = bench_ours(args, rank, world, device)
@@ -467,10 +639,28 @@ def main():
                               "per step: [peer reduce 1] + vhat partial 1 + finish 1 + step 1 + rebalance 2; "
                               "plus NCCL collectives (not counted)"),
     })
+    if world == 1:
+        bms, fms = backward_time(args.rows, args.cols, device)
+        d["backward"] = {"ms": bms, "forward_ms": fms, "tokens": M,
+                         "gemm_tflops": 2 * 2.0 * M * args.rows * args.cols / (bms * 1e-3) / 1e12,
+                         "packed_path_share": ms_share(r["ms"], bms),
+                         "note": "loss.backward() of one bare layer through the drop-in API: dX and dW "
+                                 "GEMMs + v-hat + packed step, then rebalance(); CUDA events, eager"}
     if not args.no_cpu_baseline:
         v1, dt = cpu_baseline(rows=2048, threads=1)
-        d["cpu_baseline"] = {"value": v1, "unit": "GB/s", "cores": 1, "kind": "port",
-                             "sample": f"2048 rows x {args.cols} cols (v-hat + step), {dt:.2f} s"}
+        port = {"value": v1, "unit": "GB/s", "cores": 1, "kind": "port",
+                "sample": f"2048 rows x {args.cols} cols (v-hat + step), {dt:.2f} s; oracle port (C restatement)"}
+        r1 = ref_cpu_rule(rows=2048, threads=1, steps=3)
+        if r1 is not None:
+            rall = ref_cpu_rule(rows=2048, threads=cores, steps=5)
+            d["cpu_baseline"] = {"value": r1[0], "unit": "GB/s", "cores": 1, "kind": "reference",
+                                 "sample": f"2048 rows x {args.cols} cols, ConcordRef.step "
+                                           f"(experiments/cpu_dynamics/concord_ref.py), {r1[1]:.3f} s/step"}
+            d["cpu_baseline_all_cores"] = {"value": rall[0], "unit": "GB/s", "cores": cores, "kind": "reference",
+                                           "sample": f"same, torch CPU on {cores} threads, {rall[1]:.3f} s/step"}
+            d["cpu_baseline_port"] = port
+        else:
+            d["cpu_baseline"] = port
     emit(d)
     if world > 1:
         dist.destroy_process_group()

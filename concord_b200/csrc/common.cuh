@@ -126,10 +126,7 @@ __device__ __forceinline__ int32_t repack(int32_t sf, int32_t ss, int32_t vs) {
     return (int32_t)((((uint32_t)sf & 0xFFFFu) << 16) | (((uint32_t)ss & 0xFFu) << 8) | ((uint32_t)vs & 0xFFu));
 }
 
-__device__ __forceinline__ int warp_max(int v) {
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
-    return v;
-}
+// max over the full warp (every lane active): one redux.sync instruction
+__device__ __forceinline__ int warp_max(int v) { return __reduce_max_sync(0xffffffffu, v); }
 
 }  // namespace concord

@@ -82,11 +82,22 @@ struct AdamwPre {
     float coh_num, coh_den;  // fixed gate: coh = coh_num / coh_den (divided later)
 };
 
-// 2^te; SAFE promises |te| <= 126, so the bits can be written directly
+// 2^te and 2^-te.  On SAFE elements (|te| <= 46) `te` holds the fp32 bits of
+// 2^te itself ((te + 127) << 23, the caller adds a per-row and a per-column
+// part), so both are one integer operation at most.
 template <bool SAFE>
 __device__ __forceinline__ float pow2_exp(int32_t te) {
-    return SAFE ? __uint_as_float((uint32_t)(te + 127) << 23) : exp2i(te);
+    return SAFE ? __uint_as_float((uint32_t)te) : exp2i(te);
 }
+template <bool SAFE>
+__device__ __forceinline__ float pow2_inv(int32_t te) {
+    return SAFE ? __uint_as_float(0x7F000000u - (uint32_t)te) : exp2i(-te);
+}
+// the SAFE encoding's per-row and per-column parts of te
+__device__ __forceinline__ int32_t safe_row_bits(int32_t row_e, int32_t mantissa_bias) {
+    return (int32_t)((uint32_t)(row_e - mantissa_bias + 127) << 23);
+}
+__device__ __forceinline__ int32_t safe_col_bits(int32_t col_e) { return (int32_t)((uint32_t)col_e << 23); }
 
 template <uint32_t FL, bool SAFE = false>
 __device__ __forceinline__ AdamwPre adamw_pre(const concord_step_params& P, int32_t packed, float g,
@@ -98,7 +109,8 @@ __device__ __forceinline__ AdamwPre adamw_pre(const concord_step_params& P, int3
     e.s_fast = packed >> 16;
     e.s_slow = shl32(packed, 16) >> 24;
     e.v_slow = shl32(packed, 24) >> 24;
-    e.te = row_e + col_e - P.mantissa_bias;
+    // SAFE: row_e / col_e arrive as safe_row_bits / safe_col_bits
+    e.te = SAFE ? row_e + col_e : row_e + col_e - P.mantissa_bias;
     e.g = g;
     e.cp = cp;
     const float scale_fwd = pow2_exp<SAFE>(e.te);
@@ -153,7 +165,7 @@ __device__ __forceinline__ ElemOut adamw_post(const concord_step_params& P, cons
     const uint32_t F = flags_of<FL>(P);
     const bool gpu = gpu_of<FL>(P);
     const float scale_fwd = pow2_exp<SAFE>(e.te);
-    const float scale_inv = pow2_exp<SAFE>(-e.te);
+    const float scale_inv = pow2_inv<SAFE>(e.te);
     const float coh = e.coh, d_fs = e.d_fs;
     int32_t s_fast = e.s_fast, s_slow = e.s_slow;
     const int32_t v_slow = e.v_slow;
@@ -251,7 +263,7 @@ __device__ __forceinline__ void adamw_post_lockstep(const concord_step_params& P
     float cpn[W];
 #pragma unroll
     for (int j = 0; j < W; ++j) {
-        const float scale_fwd = pow2_exp<true>(e[j].te), scale_inv = pow2_exp<true>(-e[j].te);
+        const float scale_fwd = pow2_exp<true>(e[j].te), scale_inv = pow2_inv<true>(e[j].te);
         float step_live = gpu ? clamp_gpu(step_div[j], -P.step_cap, P.step_cap) : clamp_np(step_div[j], P.step_cap);
         float evap_rate = 0.0f;   // evaporation = evap_rate * d_fs
         if (consol) evap_rate = S.lr * P.gf_consol * (1.0f - e[j].coh);
@@ -442,8 +454,14 @@ constexpr int VEC = 4;                 // consecutive columns per thread
 constexpr int STEP_COLS = 32 * VEC;    // columns per block (one warp-width)
 // elements computed in lockstep (divides VEC): two pairs keep the kernel at
 // 128 registers without spills; one quad spilled
-constexpr int STEP_LOCK = 2;
-constexpr int STEP_ROWS = 32;          // rows per block (8 per warp); fewer on small layers
+#ifndef CONCORD_STEP_LOCK
+#define CONCORD_STEP_LOCK 2
+#endif
+constexpr int STEP_LOCK = CONCORD_STEP_LOCK;
+#ifndef CONCORD_STEP_ROWS
+#define CONCORD_STEP_ROWS 32
+#endif
+constexpr int STEP_ROWS = CONCORD_STEP_ROWS;          // rows per block (8 per warp); fewer on small layers
 
 __device__ __forceinline__ void block_add_coh(double csum, double ccnt, double* coh_stats) {
     __shared__ double red[2][STEP_THREADS / 32];
@@ -510,6 +528,9 @@ __global__ void __launch_bounds__(STEP_THREADS, MINB) step_vec_kernel(StepArgs A
     bool cols_safe = true;
 #pragma unroll
     for (int j = 0; j < VEC; ++j) cols_safe &= (uint32_t)(ce[j] + 23) <= 46u;
+    int32_t cbits[VEC];
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) cbits[j] = safe_col_bits(ce[j]);
     float csum = 0.0f;
     int ccnt = 0;
     // rows of this warp: rbase + warp + 8 i; the next row's inputs are loaded
@@ -551,6 +572,7 @@ __global__ void __launch_bounds__(STEP_THREADS, MINB) step_vec_kernel(StepArgs A
             ElemOut outs[VEC];
             // SAFE rows: |te| <= 46, so 2^te and the products it scales stay finite
             const bool safe = cols_safe && (uint32_t)(re - A.P.mantissa_bias + 23) <= 46u;
+            const int32_t rbits = safe_row_bits(re, A.P.mantissa_bias);
             if (KIND == CONCORD_KIND_ADAMW && !safe) {
 #pragma unroll
                 for (int j = 0; j < VEC; ++j) {
@@ -571,7 +593,7 @@ __global__ void __launch_bounds__(STEP_THREADS, MINB) step_vec_kernel(StepArgs A
                     for (int u = 0; u < STEP_LOCK; ++u) {
                         const int j = h + u;
                         const float g = bf16_to_f32((gw[j >> 1] >> ((j & 1) * 16)) & 0xffffu);
-                        pre[u] = adamw_pre<FL, true>(A.P, wv[j], g, re, ce[j], vr, vc[j], cp[j], S);
+                        pre[u] = adamw_pre<FL, true>(A.P, wv[j], g, rbits, cbits[j], vr, vc[j], cp[j], S);
                         xs[u] = pre[u].x;
                     }
 #pragma unroll

@@ -107,7 +107,7 @@ def grads(step, rank):
     return (torch.randn(N, K, generator=g) * 1e-3).to(torch.bfloat16)
 
 
-def _worker(rank, world, port, out_dir):
+def _worker(rank, world, port, out_dir, mode="manual"):
     import sys
     sys.path.insert(0, ROOT)
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -116,10 +116,21 @@ def _worker(rank, world, port, out_dir):
     from concord_b200.distributed import RowShardedStep
     L = make_layer()
     st = RowShardedStep(L, kernels=OracleKernels())
+    from concord_b200 import packed_b as pb
     for s in range(3):
-        st.step(grads(s, rank))
-        st.rebalance()
+        if mode == "manual":
+            st.step(grads(s, rank))
+            st.rebalance()
+        else:
+            # what the layer's autograd backward and rebalance() do once the
+            # layer is registered as data-parallel
+            pb._optimizer_half(SimpleNamespace(packed_w=L.packed_w), grads(s, rank))
+            pb.ConcordLinearPackedB.rebalance(L)
     st.gather_state()
+    if mode != "manual":
+        assert pb._sharded_of(L.packed_w) is st
+        st.close()
+        assert pb._sharded_of(L.packed_w) is None
     wbuf, rmax, cmax = L._ensure_buffers()
     np.savez(os.path.join(out_dir, f"rank{rank}.npz"), packed=L.packed_w.numpy(),
              v_row=L.v_row.numpy(), v_col=L.v_col.numpy(), svi=L._sum_v_inv.numpy(),
@@ -178,9 +189,16 @@ def _free_port():
     return p
 
 
-def test_row_sharded_step_two_ranks(tmp_path, oracle_mod):
+import pytest  # noqa: E402
+
+
+@pytest.mark.parametrize("mode", ["manual", "backward"])
+def test_row_sharded_step_two_ranks(tmp_path, oracle_mod, mode):
+    """`manual`: the caller hands each rank's dW to RowShardedStep.step.
+    `backward`: the layer's own backward path (registered as data-parallel)
+    hands it over; both must give the same sharded state."""
     world = 2
-    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path), mode), nprocs=world,
                        join=True, start_method="spawn")
     r = [dict(np.load(tmp_path / f"rank{i}.npz")) for i in range(world)]
     ref = emulate(world)

@@ -28,6 +28,21 @@ def _grad(N, step, rank, dev):
     return (torch.randn(N, K, generator=g) * 3e-2).to(torch.bfloat16).to(dev)
 
 
+def _xy(N, step, rank, dev, M=64):
+    """This rank's input and upstream gradient for one step (the DP-backward tests)."""
+    g = torch.Generator(device="cpu").manual_seed(7000 + 1000 * step + rank)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16).to(dev)
+    gy = (torch.randn(M, N, generator=g) * 0.1).to(torch.bfloat16).to(dev)
+    return x, gy
+
+
+def _grad_bwd(N, step, rank, dev):
+    """The dW the layer's backward computes from _xy (the same GEMM)."""
+    from concord_b200 import gemm
+    x, gy = _xy(N, step, rank, dev)
+    return gemm.grad_weight(gy, x)
+
+
 def _layer(N, dev):
     from concord_b200 import ConcordLinearPackedB
     torch.manual_seed(5)
@@ -45,7 +60,7 @@ def _state(layer):
     return out
 
 
-def _worker(rank, world, port, out_dir, N, transport):
+def _worker(rank, world, port, out_dir, N, transport, via_backward=False):
     import sys
     sys.path.insert(0, ROOT)
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -57,8 +72,14 @@ def _worker(rank, world, port, out_dir, N, transport):
     st = RowShardedStep(layer, transport=transport)
     assert st.transport == transport
     for s in range(STEPS):
-        st.step(_grad(N, s, rank, dev))
-        st.rebalance()
+        if via_backward:
+            # the drop-in path: the registered layer's backward steps its shard
+            x, gy = _xy(N, s, rank, dev)
+            layer(x.requires_grad_(True)).backward(gy)
+            layer.rebalance()
+        else:
+            st.step(_grad(N, s, rank, dev))
+            st.rebalance()
     st.check()
     st.gather_state()
     torch.cuda.synchronize()
@@ -68,7 +89,7 @@ def _worker(rank, world, port, out_dir, N, transport):
     dist.destroy_process_group()
 
 
-def _emulate(world, N):
+def _emulate(world, N, grad_fn=_grad):
     """The same sharded arithmetic on one GPU, shard by shard."""
     from concord_b200 import packed_b as pb
     from concord_b200.distributed import CudaKernels as KK
@@ -80,9 +101,9 @@ def _emulate(world, N):
     salt = pb._get_step_counter(dev)
     salt.zero_()          # the workers' counters start at 0 in fresh processes
     for s in range(STEPS):
-        tot = _grad(N, s, 0, dev).float()
+        tot = grad_fn(N, s, 0, dev).float()
         for r in range(1, world):
-            tot = tot + _grad(N, s, r, dev).float()
+            tot = tot + grad_fn(N, s, r, dev).float()
         g = tot.to(torch.bfloat16)
         acc = torch.zeros(K + 1, dtype=torch.float32, device=dev)
         for r in range(world):
@@ -126,6 +147,26 @@ def test_row_sharded_step(tmp_path, N, world, transport):
                        nprocs=world, join=True, start_method="spawn")
     r = [dict(np.load(tmp_path / f"rank{i}.npz")) for i in range(world)]
     ref = _emulate(world, N)
+    for key in ref:
+        for i in range(1, world):
+            np.testing.assert_array_equal(r[0][key], r[i][key], err_msg=key)
+        np.testing.assert_array_equal(r[0][key], ref[key], err_msg=key)
+
+
+@pytest.mark.parametrize("world,transport", [(2, "collective"), (2, "peer")])
+def test_data_parallel_through_loss_backward(tmp_path, world, transport):
+    """Data-parallel training through the drop-in API: each rank calls
+    layer(x).backward(dY) and layer.rebalance() on its own batch; the layer,
+    registered with a RowShardedStep, steps only its row shard of the reduced
+    gradient.  Every rank ends identical and equal to the one-GPU emulation
+    fed the ranks' dW (no local step happened on the way)."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    N = 304
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path), N, transport, True),
+                       nprocs=world, join=True, start_method="spawn")
+    r = [dict(np.load(tmp_path / f"rank{i}.npz")) for i in range(world)]
+    ref = _emulate(world, N, grad_fn=_grad_bwd)
     for key in ref:
         for i in range(1, world):
             np.testing.assert_array_equal(r[0][key], r[i][key], err_msg=key)

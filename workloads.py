@@ -1,0 +1,297 @@
+"""Synthetic training workloads of the benchmark configurations that run
+whole models, built in plain torch with Concord on
+their weight matrices.  Random init and seeded synthetic data: no dataset or
+checkpoint is read.
+
+* Config 3, char-level GPT: the reference's nanoGPT architecture
+  (notebook/src/nanogpt.py:15-101: pre-LN blocks, bias-free Linears, GELU
+  MLP, learned positions, causal SDPA), 6 layers, 6 heads, d=384, context
+  256, vocab 65, batch 64, on tokens from a seeded order-2 Markov chain over
+  65 symbols whose transition rows are Dirichlet(0.3).
+* Config 5, Llama-style decoder (24 layers, d=2048, 16 heads, SwiGLU 5504,
+  vocab 32000, seq 2048) on uniform random token ids.
+"""
+import math
+import time
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+
+# ---------------------------------------------------------------- data
+class MarkovChars:
+    """Order-2 Markov chain over `vocab` symbols, transition rows ~ Dirichlet(alpha).
+
+    Generates `n_chains` independent chains of `length` tokens on the device
+    (vectorised over chains) and serves random windows of them."""
+
+    def __init__(self, vocab=65, alpha=0.3, n_chains=4096, length=1024, seed=0, device="cuda"):
+        g = torch.Generator().manual_seed(seed)
+        conc = torch.full((vocab,), float(alpha))
+        self.P = torch.distributions.Dirichlet(conc).sample((vocab * vocab,)).to(device)  # [V*V, V]
+        gd = torch.Generator(device=device).manual_seed(seed + 1)
+        toks = torch.empty(n_chains, length, dtype=torch.long, device=device)
+        toks[:, :2] = torch.randint(0, vocab, (n_chains, 2), generator=gd, device=device)
+        cdf = self.P.cumsum(dim=1)
+        cdf[:, -1] = 1.0
+        for t in range(2, length):
+            state = toks[:, t - 2] * vocab + toks[:, t - 1]
+            u = torch.rand(n_chains, 1, generator=gd, device=device)
+            toks[:, t] = torch.searchsorted(cdf[state], u).squeeze(1).clamp_(max=vocab - 1)
+        self.toks, self.vocab, self.gen = toks, vocab, torch.Generator(device=device).manual_seed(seed + 2)
+
+    def entropy_rate(self):
+        """Mean next-token entropy (nats) under the chain's empirical pair
+        frequencies: the loss floor a perfect model reaches."""
+        V = self.vocab
+        pair = self.toks[:, :-1] * V + self.toks[:, 1:]
+        freq = torch.bincount(pair[:, 1:].reshape(-1), minlength=V * V).float()   # states after burn-in
+        freq = freq / freq.sum()
+        h = -(self.P.clamp_min(1e-30) * self.P.clamp_min(1e-30).log()).sum(dim=1)
+        return float((freq * h).sum())
+
+    def batch(self, B, T):
+        n, L = self.toks.shape
+        c = torch.randint(0, n, (B,), generator=self.gen, device=self.toks.device)
+        o = torch.randint(0, L - T - 1, (B,), generator=self.gen, device=self.toks.device)
+        idx = o[:, None] + torch.arange(T + 1, device=self.toks.device)[None, :]
+        w = self.toks[c[:, None], idx]
+        return w[:, :-1], w[:, 1:]
+
+
+# ---------------------------------------------------------------- config 3: char GPT
+class CausalSelfAttention(nn.Module):
+    def __init__(self, d, h):
+        super().__init__()
+        self.c_attn = nn.Linear(d, 3 * d, bias=False)
+        self.c_proj = nn.Linear(d, d, bias=False)
+        self.h, self.d = h, d
+
+    def forward(self, x):
+        B, T, C = x.shape
+        q, k, v = self.c_attn(x).split(self.d, dim=2)
+        q, k, v = (t.view(B, T, self.h, C // self.h).transpose(1, 2) for t in (q, k, v))
+        y = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+        return self.c_proj(y.transpose(1, 2).reshape(B, T, C))
+
+
+class GPTBlock(nn.Module):
+    def __init__(self, d, h):
+        super().__init__()
+        self.ln_1, self.ln_2 = nn.LayerNorm(d), nn.LayerNorm(d)
+        self.attn = CausalSelfAttention(d, h)
+        self.c_fc = nn.Linear(d, 4 * d, bias=False)
+        self.mlp_proj = nn.Linear(4 * d, d, bias=False)
+
+    def forward(self, x):
+        x = x + self.attn(self.ln_1(x))
+        return x + self.mlp_proj(F.gelu(self.c_fc(self.ln_2(x))))
+
+
+class CharGPT(nn.Module):
+    def __init__(self, vocab=65, block=256, n_layer=6, n_head=6, d=384):
+        super().__init__()
+        self.wte, self.wpe = nn.Embedding(vocab, d), nn.Embedding(block, d)
+        self.blocks = nn.ModuleList([GPTBlock(d, n_head) for _ in range(n_layer)])
+        self.ln_f = nn.LayerNorm(d)
+        self.lm_head = nn.Linear(d, vocab, bias=False)
+        for m in self.modules():
+            if isinstance(m, (nn.Linear, nn.Embedding)):
+                nn.init.normal_(m.weight, 0.0, 0.02)
+        for b in self.blocks:   # nanoGPT's residual-projection scaling
+            for lin in (b.attn.c_proj, b.mlp_proj):
+                nn.init.normal_(lin.weight, 0.0, 0.02 / math.sqrt(2 * n_layer))
+
+    def forward(self, idx, targets):
+        T = idx.shape[1]
+        x = self.wte(idx) + self.wpe(torch.arange(T, device=idx.device))[None]
+        for b in self.blocks:
+            x = b(x)
+        logits = self.lm_head(self.ln_f(x)).float()
+        return F.cross_entropy(logits.view(-1, logits.shape[-1]), targets.reshape(-1))
+
+
+def lr_at(it, peak, warmup, total, floor=0.1):
+    if it < warmup:
+        return peak * (it + 1) / warmup
+    p = (it - warmup) / max(1, total - warmup)
+    return peak * (floor + (1 - floor) * 0.5 * (1 + math.cos(math.pi * p)))
+
+
+def train_chargpt(steps=2000, batch=64, block=256, lr=5e-4, aux_lr=0.05, seed=0, device="cuda",
+                  log_every=100, warmup=100):
+    """Config 3 on one GPU.  Concord on every Linear (self-stepping backward,
+    rebalance every step), SGD with momentum 0.9 on embeddings and norms,
+    bf16 autocast.  Returns losses, timings and the chain's entropy floor."""
+    from concord_b200.convert import aux_parameters, concordify
+    torch.manual_seed(seed)
+    data = MarkovChars(seed=seed, device=device)
+    model = CharGPT(block=block).to(device)
+    layers = concordify(model, lr=lr)
+    aux = torch.optim.SGD(aux_parameters(model), lr=aux_lr, momentum=0.9)
+    n_concord = sum(l.packed_w.numel() for l in layers)
+    n_aux = sum(p.numel() for p in aux_parameters(model))
+    log, t_train = [], 0.0
+    for it in range(steps):
+        cur = lr_at(it, lr, warmup, steps)
+        for l in layers:
+            l.lr = cur
+        for grp in aux.param_groups:
+            grp["lr"] = lr_at(it, aux_lr, warmup, steps)
+        x, y = data.batch(batch, block)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = model(x, y)
+        loss.backward()               # Concord layers step inside the backward
+        aux.step()
+        aux.zero_grad(set_to_none=True)
+        for l in layers:
+            l.rebalance()
+        torch.cuda.synchronize()
+        if it >= 10:
+            t_train += time.perf_counter() - t0
+        if it % log_every == 0 or it == steps - 1:
+            log.append((it, float(loss.item())))
+    return dict(losses=log, steps_per_s=(steps - 10) / t_train, concord_params=n_concord, aux_params=n_aux,
+                entropy_floor=data.entropy_rate(), tokens_per_step=batch * block)
+
+
+# ---------------------------------------------------------------- config 5: Llama-style decoder
+class RMSNorm(nn.Module):
+    def __init__(self, d, eps=1e-5):
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(d))
+        self.eps = eps
+
+    def forward(self, x):
+        xf = x.float()
+        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps) * self.weight).to(x.dtype)
+
+
+def rope_tables(T, hd, device, base=10000.0):
+    inv = 1.0 / (base ** (torch.arange(0, hd, 2, device=device).float() / hd))
+    f = torch.outer(torch.arange(T, device=device).float(), inv)
+    return f.cos().to(torch.bfloat16), f.sin().to(torch.bfloat16)
+
+
+def apply_rope(x, cos, sin):
+    x1, x2 = x[..., 0::2], x[..., 1::2]
+    return torch.stack((x1 * cos - x2 * sin, x1 * sin + x2 * cos), dim=-1).flatten(-2)
+
+
+class LlamaBlock(nn.Module):
+    def __init__(self, d, h, ffn):
+        super().__init__()
+        self.h = h
+        self.attn_norm, self.ffn_norm = RMSNorm(d), RMSNorm(d)
+        self.wq, self.wk, self.wv, self.wo = (nn.Linear(d, d, bias=False) for _ in range(4))
+        self.w_gate, self.w_up = nn.Linear(d, ffn, bias=False), nn.Linear(d, ffn, bias=False)
+        self.w_down = nn.Linear(ffn, d, bias=False)
+
+    def forward(self, x, cos, sin):
+        B, T, D = x.shape
+        a = self.attn_norm(x)
+        q, k, v = (lin(a).view(B, T, self.h, D // self.h).transpose(1, 2) for lin in (self.wq, self.wk, self.wv))
+        q, k = apply_rope(q, cos, sin), apply_rope(k, cos, sin)
+        y = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+        x = x + self.wo(y.transpose(1, 2).reshape(B, T, D))
+        f = self.ffn_norm(x)
+        return x + self.w_down(F.silu(self.w_gate(f)) * self.w_up(f))
+
+
+class Llama(nn.Module):
+    def __init__(self, vocab=32000, d=2048, n_layer=24, n_head=16, ffn=5504):
+        super().__init__()
+        self.emb = nn.Embedding(vocab, d)
+        self.blocks = nn.ModuleList([LlamaBlock(d, n_head, ffn) for _ in range(n_layer)])
+        self.norm = RMSNorm(d)
+        self.lm_head = nn.Linear(d, vocab, bias=False)
+        self.hd = d // n_head
+        for m in self.modules():
+            if isinstance(m, (nn.Linear, nn.Embedding)):
+                nn.init.normal_(m.weight, 0.0, 0.02)
+
+    def forward(self, idx, targets):
+        T = idx.shape[1]
+        cos, sin = rope_tables(T, self.hd, idx.device)
+        x = self.emb(idx)
+        for b in self.blocks:
+            x = b(x, cos, sin)
+        logits = self.lm_head(self.norm(x))
+        return F.cross_entropy(logits.float().view(-1, logits.shape[-1]), targets.reshape(-1))
+
+
+def train_llama_dp(steps, warmup, batch_per_gpu=8, seq=2048, lr=5e-4, aux_lr=0.01, seed=0, n_layer=24,
+                   group=None):
+    """Config 5: data-parallel training steps of the Llama-style decoder, one
+    process per GPU (torch.distributed already initialised when world > 1).
+
+    Weak scaling: each rank trains on its own `batch_per_gpu` sequences of
+    uniform random token ids (global batch = world * batch_per_gpu; 64 at 8
+    GPUs).  Concord on the 168 block Linears; on more than one rank each is
+    registered with a RowShardedStep, so `loss.backward()` reduce-scatters
+    every layer's dW over NVLink, steps the rank's row shard and all-gathers
+    the bf16 forward weight.  Embedding, norms and lm_head take SGD (momentum
+    0.9) on gradients all-reduced in one bucket.  Returns per-step device
+    times (max over ranks) and the loss."""
+    import torch.distributed as dist
+    from concord_b200.convert import concordify
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    rank = dist.get_rank(group) if dist.is_initialized() else 0
+    dev = torch.device("cuda", torch.cuda.current_device())
+    torch.manual_seed(seed)
+    model = Llama(n_layer=n_layer).to(dev)
+    layers = concordify(model, lr=lr, skip=lambda name, m: name == "lm_head")
+    steppers = []
+    if world > 1:
+        from concord_b200.distributed import RowShardedStep
+        steppers = [RowShardedStep(l, group=group) for l in layers]
+    aux = [p for p in model.parameters() if p.requires_grad]
+    opt = torch.optim.SGD(aux, lr=aux_lr, momentum=0.9)
+    flat = torch.zeros(sum(p.numel() for p in aux), dtype=torch.float32, device=dev)
+    g = torch.Generator(device=dev).manual_seed(seed * 1000 + rank)
+    times, losses = [], []
+    for it in range(warmup + steps):
+        x = torch.randint(0, 32000, (batch_per_gpu, seq + 1), generator=g, device=dev)
+        if world > 1:
+            dist.barrier(group=group)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = model(x[:, :-1], x[:, 1:])
+        loss.backward()                       # every Concord layer steps (its shard) here
+        if world > 1:                         # the ordinary parameters: one bucketed all-reduce
+            off = 0
+            for p in aux:
+                flat[off:off + p.numel()].copy_(p.grad.view(-1))
+                off += p.numel()
+            dist.all_reduce(flat, group=group)
+            flat.div_(world)
+            off = 0
+            for p in aux:
+                p.grad.view(-1).copy_(flat[off:off + p.numel()])
+                off += p.numel()
+        opt.step()
+        opt.zero_grad(set_to_none=False)
+        for l in layers:
+            l.rebalance()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+            ms = float(t.item())
+        if it >= warmup:
+            times.append(ms)
+        losses.append(float(loss.item()))
+    for st in steppers:
+        st.check()
+    params = sum(l.packed_w.numel() for l in layers)
+    for st in steppers:
+        st.close()
+    return dict(ms=times, losses=losses, concord_params=params, world=world,
+                tokens_per_step=world * batch_per_gpu * seq)
