@@ -295,3 +295,236 @@ def train_llama_dp(steps, warmup, batch_per_gpu=8, seq=2048, lr=5e-4, aux_lr=0.0
         st.close()
     return dict(ms=times, losses=losses, concord_params=params, world=world,
                 tokens_per_step=world * batch_per_gpu * seq)
+
+
+# ---------------------------------------------------------------- config 4: SDXL-architecture UNet
+# The public SDXL UNet layout (diffusers UNet2DConditionModel as configured for
+# SDXL base): channels (320, 640, 1280), two ResNet blocks per level, linear
+# projections in and out of the transformers, transformer depth (0, 2, 10)
+# with 64-dim heads, cross-attention to a 2048-wide text context, and the
+# "text_time" additional embedding (pooled text 1280 + six 256-dim Fourier
+# time ids).  Written here from that public description; random init.
+def timestep_features(t, dim, max_period=10000.0):
+    half = dim // 2
+    freqs = torch.exp(-math.log(max_period) * torch.arange(half, device=t.device, dtype=torch.float32) / half)
+    a = t.float()[:, None] * freqs[None]
+    return torch.cat([torch.cos(a), torch.sin(a)], dim=-1)
+
+
+class ResBlock(nn.Module):
+    def __init__(self, cin, cout, temb=1280):
+        super().__init__()
+        self.norm1, self.norm2 = nn.GroupNorm(32, cin, eps=1e-5), nn.GroupNorm(32, cout, eps=1e-5)
+        self.conv1, self.conv2 = nn.Conv2d(cin, cout, 3, padding=1), nn.Conv2d(cout, cout, 3, padding=1)
+        self.time_emb_proj = nn.Linear(temb, cout)
+        self.conv_shortcut = nn.Conv2d(cin, cout, 1) if cin != cout else None
+
+    def forward(self, x, emb):
+        h = self.conv1(F.silu(self.norm1(x)))
+        h = h + self.time_emb_proj(F.silu(emb))[:, :, None, None].to(h.dtype)
+        h = self.conv2(F.silu(self.norm2(h)))
+        return (x if self.conv_shortcut is None else self.conv_shortcut(x)) + h
+
+
+class Attention(nn.Module):
+    def __init__(self, c, ctx=None, head_dim=64):
+        super().__init__()
+        kv = ctx or c
+        self.heads = c // head_dim
+        self.to_q, self.to_k, self.to_v = nn.Linear(c, c, bias=False), nn.Linear(kv, c, bias=False), nn.Linear(kv, c, bias=False)
+        self.to_out = nn.Linear(c, c)
+
+    def forward(self, x, ctx=None):
+        B, T, C = x.shape
+        src = x if ctx is None else ctx
+        q = self.to_q(x).view(B, T, self.heads, -1).transpose(1, 2)
+        k = self.to_k(src).view(B, src.shape[1], self.heads, -1).transpose(1, 2)
+        v = self.to_v(src).view(B, src.shape[1], self.heads, -1).transpose(1, 2)
+        y = F.scaled_dot_product_attention(q, k, v)
+        return self.to_out(y.transpose(1, 2).reshape(B, T, C))
+
+
+class TransformerBlock(nn.Module):
+    def __init__(self, c, ctx):
+        super().__init__()
+        self.norm1, self.norm2, self.norm3 = nn.LayerNorm(c), nn.LayerNorm(c), nn.LayerNorm(c)
+        self.attn1, self.attn2 = Attention(c), Attention(c, ctx)
+        self.ff_proj = nn.Linear(c, 8 * c)          # GEGLU: value and gate halves
+        self.ff_out = nn.Linear(4 * c, c)
+
+    def forward(self, x, ctx):
+        x = x + self.attn1(self.norm1(x))
+        x = x + self.attn2(self.norm2(x), ctx)
+        a, gate = self.ff_proj(self.norm3(x)).chunk(2, dim=-1)
+        return x + self.ff_out(a * F.gelu(gate))
+
+
+class Transformer2D(nn.Module):
+    def __init__(self, c, depth, ctx=2048):
+        super().__init__()
+        self.norm = nn.GroupNorm(32, c, eps=1e-6)
+        self.proj_in, self.proj_out = nn.Linear(c, c), nn.Linear(c, c)
+        self.blocks = nn.ModuleList([TransformerBlock(c, ctx) for _ in range(depth)])
+
+    def forward(self, x, ctx):
+        B, C, H, W = x.shape
+        h = self.proj_in(self.norm(x).permute(0, 2, 3, 1).reshape(B, H * W, C))
+        for b in self.blocks:
+            h = b(h, ctx)
+        return x + self.proj_out(h).reshape(B, H, W, C).permute(0, 3, 1, 2).to(x.dtype)
+
+
+class SDXLUNet(nn.Module):
+    def __init__(self, ch=(320, 640, 1280), depth=(0, 2, 10), ctx=2048, pooled=1280, in_ch=4):
+        super().__init__()
+        c0, c1, c2 = ch
+        temb = 4 * c0
+        self.time_lin1, self.time_lin2 = nn.Linear(c0, temb), nn.Linear(temb, temb)
+        self.add_lin1, self.add_lin2 = nn.Linear(pooled + 6 * 256, temb), nn.Linear(temb, temb)
+        self.conv_in = nn.Conv2d(in_ch, c0, 3, padding=1)
+        self.down = nn.ModuleList()
+        skips, prev = [c0], c0
+        for lvl, (c, d) in enumerate(zip(ch, depth)):
+            blk = nn.Module()
+            blk.res = nn.ModuleList([ResBlock(prev if i == 0 else c, c, temb) for i in range(2)])
+            blk.attn = nn.ModuleList([Transformer2D(c, d, ctx) for _ in range(2)]) if d else None
+            skips += [c, c]
+            blk.downsample = nn.Conv2d(c, c, 3, stride=2, padding=1) if lvl < len(ch) - 1 else None
+            if blk.downsample is not None:
+                skips.append(c)
+            self.down.append(blk)
+            prev = c
+        self.mid_res1, self.mid_attn, self.mid_res2 = (ResBlock(c2, c2, temb), Transformer2D(c2, depth[-1], ctx),
+                                                      ResBlock(c2, c2, temb))
+        self.up = nn.ModuleList()
+        for lvl, (c, d) in enumerate(zip(reversed(ch), reversed(depth))):
+            blk = nn.Module()
+            res = []
+            for i in range(3):
+                res.append(ResBlock(prev + skips.pop(), c, temb))
+                prev = c
+            blk.res = nn.ModuleList(res)
+            blk.attn = nn.ModuleList([Transformer2D(c, d, ctx) for _ in range(3)]) if d else None
+            blk.upsample = nn.Conv2d(c, c, 3, padding=1) if lvl < len(ch) - 1 else None
+            self.up.append(blk)
+        self.norm_out = nn.GroupNorm(32, c0, eps=1e-5)
+        self.conv_out = nn.Conv2d(c0, in_ch, 3, padding=1)
+
+    def forward(self, x, t, ctx, pooled, time_ids):
+        emb = self.time_lin2(F.silu(self.time_lin1(timestep_features(t, self.time_lin1.in_features))))
+        tid = timestep_features(time_ids.reshape(-1), 256).reshape(x.shape[0], -1)
+        add = self.add_lin2(F.silu(self.add_lin1(torch.cat([pooled, tid.to(pooled.dtype)], dim=-1))))
+        emb = emb + add
+        h = self.conv_in(x)
+        skips = [h]
+        for blk in self.down:
+            for i, r in enumerate(blk.res):
+                h = r(h, emb)
+                if blk.attn is not None:
+                    h = blk.attn[i](h, ctx)
+                skips.append(h)
+            if blk.downsample is not None:
+                h = blk.downsample(h)
+                skips.append(h)
+        h = self.mid_res2(self.mid_attn(self.mid_res1(h, emb), ctx), emb)
+        for blk in self.up:
+            for i, r in enumerate(blk.res):
+                h = r(torch.cat([h, skips.pop().to(h.dtype)], dim=1), emb)
+                if blk.attn is not None:
+                    h = blk.attn[i](h, ctx)
+            if blk.upsample is not None:
+                h = blk.upsample(F.interpolate(h, scale_factor=2.0, mode="nearest"))
+        return self.conv_out(F.silu(self.norm_out(h)))
+
+
+def sdxl_batch(B, gen, device, res=128):
+    """Config 4's synthetic batch: latents [B,4,res,res], context [B,77,2048],
+    pooled [B,1280] ~ N(0,1), timesteps U{0..999}, noise target."""
+    lat = torch.randn(B, 4, res, res, generator=gen, device=device)
+    ctx = torch.randn(B, 77, 2048, generator=gen, device=device)
+    pooled = torch.randn(B, 1280, generator=gen, device=device)
+    t = torch.randint(0, 1000, (B,), generator=gen, device=device)
+    noise = torch.randn(B, 4, res, res, generator=gen, device=device)
+    ids = torch.tensor([1024.0, 1024.0, 0.0, 0.0, 1024.0, 1024.0], device=device).repeat(B, 1)
+    return lat, ctx, pooled, t, noise, ids
+
+
+def train_sdxl_dp(steps, warmup, batch_per_gpu=4, res=128, lr=5e-4, aux_lr=1e-3, seed=0, group=None,
+                  gate=True):
+    """Config 4: epsilon-prediction MSE fine-tune steps of the SDXL-architecture
+    UNet (~2.6 B parameters, random init), bf16 autocast, Concord on every
+    Linear and every convolution (3x3 ones as their reshaped [O, I*9] weight),
+    SGD (momentum 0.9) on norms and biases.  One process per GPU; with more
+    than one rank every packed layer is data-parallel (RowShardedStep inside
+    loss.backward()) and the other parameters' gradients are all-reduced.
+    Weak scaling: `batch_per_gpu` samples per GPU."""
+    import torch.distributed as dist
+    from concord_b200.convert import concordify
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    rank = dist.get_rank(group) if dist.is_initialized() else 0
+    dev = torch.device("cuda", torch.cuda.current_device())
+    torch.manual_seed(seed)
+    model = SDXLUNet().to(dev)
+    n_total = sum(p.numel() for p in model.parameters())
+    layers = concordify(model, lr=lr, convs=True)
+    if not gate:
+        for l in layers:
+            l.disable_cohpre()
+    steppers = []
+    if world > 1:
+        from concord_b200.distributed import RowShardedStep
+        steppers = [RowShardedStep(l, group=group) for l in layers]
+    aux = [p for p in model.parameters() if p.requires_grad]
+    opt = torch.optim.SGD(aux, lr=aux_lr, momentum=0.9)
+    flat = torch.zeros(sum(p.numel() for p in aux), dtype=torch.float32, device=dev)
+    g = torch.Generator(device=dev).manual_seed(seed * 1000 + rank)
+    torch.cuda.synchronize()
+    base_mem = torch.cuda.memory_allocated()
+    torch.cuda.reset_peak_memory_stats()
+    times, losses = [], []
+    for it in range(warmup + steps):
+        lat, ctx, pooled, t, noise, ids = sdxl_batch(batch_per_gpu, g, dev, res)
+        alpha_bar = torch.cos(t.float() / 1000 * math.pi / 2) ** 2
+        noisy = alpha_bar.sqrt()[:, None, None, None] * lat + (1 - alpha_bar).sqrt()[:, None, None, None] * noise
+        if world > 1:
+            dist.barrier(group=group)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            pred = model(noisy, t, ctx, pooled, ids)
+        loss = F.mse_loss(pred.float(), noise)
+        loss.backward()
+        if world > 1:
+            off = 0
+            for p in aux:
+                flat[off:off + p.numel()].copy_(p.grad.view(-1))
+                off += p.numel()
+            dist.all_reduce(flat, group=group)
+            flat.div_(world)
+            off = 0
+            for p in aux:
+                p.grad.view(-1).copy_(flat[off:off + p.numel()])
+                off += p.numel()
+        opt.step()
+        opt.zero_grad(set_to_none=False)
+        for l in layers:
+            l.rebalance()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            tt = torch.tensor([ms], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX, group=group)
+            ms = float(tt.item())
+        if it >= warmup:
+            times.append(ms)
+        losses.append(float(loss.item()))
+    for st in steppers:
+        st.check()
+    out = dict(ms=times, losses=losses, params=n_total, concord_params=sum(l.packed_w.numel() for l in layers),
+               n_layers=len(layers), world=world, samples_per_step=world * batch_per_gpu,
+               state_gb=base_mem / 1e9, peak_gb=torch.cuda.max_memory_allocated() / 1e9)
+    for st in steppers:
+        st.close()
+    return out
