@@ -460,17 +460,19 @@ def bench_chargpt(args, cores):
     import workloads
     steps = args.steps
     torch.cuda.reset_peak_memory_stats()
-    r = workloads.train_chargpt(steps=steps)
+    r = workloads.train_chargpt(steps=steps, graph=args.graph)
     d = {"metric": "char-GPT (config 3) train steps/s", "unit": "steps/s", "n_gpus": 1, "steps": steps,
          "warmup": 10, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
          "dtype": "bf16 autocast; packed int32 words", "data": "synthetic: order-2 Markov chain, 65 symbols, "
          "Dirichlet(0.3) rows, seed 0", "config": {"workload": "config 3: 6L/6H/384d char-GPT, ctx 256, batch 64, "
          "Concord on all Linears, SGD(0.9) on embeddings/norms, lr 5e-4", "seq_len": 256, "global_batch": 64},
-         "value": r["steps_per_s"], "ms_per_step": 1e3 / r["steps_per_s"],
+         "value": r["steps_per_s"], "ms_per_step": r["ms_per_step"],
          "tokens_per_s": r["steps_per_s"] * r["tokens_per_step"], "losses": r["losses"],
          "entropy_floor_nats": r["entropy_floor"], "concord_params": r["concord_params"],
          "aux_params": r["aux_params"], "peak_mem_gb": torch.cuda.max_memory_allocated() / 1e9,
-         "timing": "host wall clock around each step with a device synchronize on both sides, steps 10.."}
+         "cuda_graph": r["cuda_graph"],
+         "timing": "CUDA events around each training step (one CUDA graph replay after 10 eager steps "
+                   "unless --no-graph), mean over steps 10.."}
     if not args.no_cpu_baseline:
         v1 = chargpt_cpu_baseline(1, steps=1)
         if v1 is not None:
@@ -486,7 +488,7 @@ def bench_llama(args, rank, world):
     import workloads
     torch.cuda.reset_peak_memory_stats()
     r = workloads.train_llama_dp(steps=args.steps, warmup=args.warmup, batch_per_gpu=args.batch,
-                                 n_layer=args.layers)
+                                 n_layer=args.layers, graph=args.graph)
     ms = statistics.mean(r["ms"])
     mem = torch.tensor([torch.cuda.max_memory_allocated() / 1e9], device="cuda")
     if world > 1:
@@ -504,7 +506,39 @@ def bench_llama(args, rank, world):
           "value": r["tokens_per_step"] / (ms * 1e-3), "ms_per_step": ms,
           "ms_per_step_all": r["ms"], "loss_first_last": [r["losses"][0], r["losses"][-1]],
           "concord_params": r["concord_params"], "peak_mem_gb_max_rank": float(mem.item()),
-          "timing": "CUDA events around forward+backward+aux step+rebalance, barrier before, max over ranks"})
+          "cuda_graph": args.graph,
+          "timing": "CUDA events around one training step (forward, backward with the packed steps, aux update, "
+                    "rebalance; replayed as one CUDA graph unless --no-graph), barrier before, max over ranks"})
+
+
+def bench_sdxl(args, rank, world):
+    """Config 4: SDXL-architecture UNet training steps, weak scaling."""
+    import workloads
+    batch = args.batch if args.batch != 8 else 4
+    r = workloads.train_sdxl_dp(steps=args.steps, warmup=args.warmup, batch_per_gpu=batch, gate=not args.nogate,
+                                ckpt=args.ckpt, graph=args.graph)
+    ms = statistics.mean(r["ms"])
+    mem = torch.tensor([r["peak_gb"], r["state_gb"]], device="cuda")
+    if world > 1:
+        dist.all_reduce(mem, op=dist.ReduceOp.MAX)
+    if rank != 0:
+        return
+    emit({"metric": "SDXL UNet train steps/s", "unit": "samples/s", "n_gpus": world, "steps": args.steps,
+          "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+          "dtype": "bf16 autocast; packed int32 words", "data": "synthetic: latents, text context, pooled ~ N(0,1), "
+          "t ~ U{0..999}, epsilon-prediction MSE",
+          "config": {"workload": f"config 4: SDXL-architecture UNet ({r['params'] / 1e9:.3f} B params, random init), "
+                                 f"latents [{batch},4,128,128] per GPU, Concord on all {r['n_layers']} Linear and conv "
+                                 f"layers ({r['concord_params'] / 1e9:.3f} B params), coh_pre gate "
+                                 f"{'off' if args.nogate else 'on'}, activation checkpointing "
+                                 f"{'on' if args.ckpt else 'off'}, lr 5e-5",
+                     "global_batch": batch * world, "parallelism": f"dp{world}"},
+          "value": r["samples_per_step"] / (ms * 1e-3), "steps_per_s": 1e3 / ms, "ms_per_step": ms,
+          "ms_per_step_all": r["ms"], "loss_first_last": [r["losses"][0], r["losses"][-1]],
+          "peak_mem_gb_max_rank": float(mem[0].item()), "state_mem_gb_max_rank": float(mem[1].item()),
+          "cuda_graph": args.graph,
+          "timing": "CUDA events around one training step (forward, backward with the packed steps, aux update, "
+                    "rebalance; replayed as one CUDA graph unless --no-graph), barrier before, max over ranks"})
 
 
 def ms_share(part, whole):
@@ -543,10 +577,13 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=8, help="llama: sequences per GPU")
     ap.add_argument("--layers", type=int, default=24, help="llama: decoder layers")
-    ap.add_argument("--workload", default="c2", choices=["c2", "chargpt", "llama"],
+    ap.add_argument("--nogate", action="store_true", help="sdxl: disable_cohpre on every layer")
+    ap.add_argument("--ckpt", action="store_true", help="sdxl: activation checkpointing per block")
+    ap.add_argument("--workload", default="c2", choices=["c2", "chargpt", "llama", "sdxl"],
                     help="c2: the packed-step path on config 2's largest layer (default); "
                          "chargpt: config 3's char-level GPT trained end to end; "
-                         "llama: config 5's data-parallel decoder (weak scaling)")
+                         "llama: config 5's data-parallel decoder (weak scaling); "
+                         "sdxl: config 4's UNet fine-tune (weak scaling)")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="time eager launches instead of CUDA-graph replays")
     args = ap.parse_args()
@@ -592,8 +629,8 @@ def main():
         torch.cuda.set_device(local)
         dist.init_process_group("nccl")
     device = torch.device("cuda", torch.cuda.current_device())
-    if args.workload == "llama":
-        bench_llama(args, rank, world)
+    if args.workload in ("llama", "sdxl"):
+        (bench_llama if args.workload == "llama" else bench_sdxl)(args, rank, world)
         if world > 1:
             dist.destroy_process_group()
         return

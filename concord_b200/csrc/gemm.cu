@@ -147,10 +147,26 @@ int dw_slices(int64_t M, int64_t N, int64_t K) {
 // current context on the calling host thread.  A thread whose first CUDA work
 // is this call (an autograd worker thread running a backward whose first node
 // is this layer, for instance) may have none bound yet; encoding then fails
-// and the kernel would run with an invalid descriptor.  Binding the current
-// device's primary context first (cudaSetDevice of the device already current)
-// rules that out without changing the caller's device.
+// and the kernel would run with an invalid descriptor.  When the thread has
+// no current context, bind the current device's primary context first
+// (cudaSetDevice of the device already current).  A thread with a context —
+// always the case while a stream capture is running — makes no call that
+// could implicitly synchronise.
+typedef int (*CuCtxGetCurrentFn)(void**);
+
 int bind_current_context(const char* name) {
+    static CuCtxGetCurrentFn get_current = [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            fn = nullptr;
+        return reinterpret_cast<CuCtxGetCurrentFn>(fn);
+    }();
+    if (get_current) {
+        void* ctx = nullptr;
+        if (get_current(&ctx) == 0 && ctx != nullptr) return CONCORD_OK;
+    }
     int dev = -1;
     cudaError_t e = cudaGetDevice(&dev);
     if (e == cudaSuccess) e = cudaSetDevice(dev);

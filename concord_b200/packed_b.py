@@ -213,12 +213,17 @@ _WORKSPACES = {}
 
 
 def _workspace(kind, nbytes, device):
-    """Zero-initialised scratch shared per (kind, device); grown on demand.
+    """Zero-initialised scratch shared per (kind, device, current stream);
+    grown on demand.
 
     The kernels leave their counters at zero after every launch, so one
-    buffer serves every layer on a device (launches on one stream are ordered).
+    buffer serves every layer launched on a stream (launches on one stream are
+    ordered).  Layers stepped on different streams get different buffers, so
+    they neither race on the counters nor free a buffer another stream still
+    reads (a replaced buffer was only ever used on this stream, and the
+    caching allocator reuses its memory in that stream's order).
     """
-    key = (kind, _dev_key(device))
+    key = (kind, _dev_key(device), torch.cuda.current_stream(device).cuda_stream)
     buf = _WORKSPACES.get(key)
     if buf is None or buf.numel() < nbytes:
         buf = torch.zeros(max(int(nbytes), 256), dtype=torch.uint8, device=device)

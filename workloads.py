@@ -120,42 +120,148 @@ def lr_at(it, peak, warmup, total, floor=0.1):
 
 
 def train_chargpt(steps=2000, batch=64, block=256, lr=5e-4, aux_lr=0.05, seed=0, device="cuda",
-                  log_every=100, warmup=100):
+                  log_every=100, warmup=100, graph=True):
     """Config 3 on one GPU.  Concord on every Linear (self-stepping backward,
     rebalance every step), SGD with momentum 0.9 on embeddings and norms,
-    bf16 autocast.  Returns losses, timings and the chain's entropy floor."""
+    bf16 autocast.  The Concord lr follows warm-up + cosine through the
+    layers' device lr scalars (so a captured graph follows it); the aux lr is
+    constant.  With `graph`, the whole training step is one CUDA graph after
+    10 eager steps.  Returns losses, timings and the chain's entropy floor."""
     from concord_b200.convert import aux_parameters, concordify
     torch.manual_seed(seed)
     data = MarkovChars(seed=seed, device=device)
     model = CharGPT(block=block).to(device)
     layers = concordify(model, lr=lr)
-    aux = torch.optim.SGD(aux_parameters(model), lr=aux_lr, momentum=0.9)
+    aux = aux_parameters(model)
+    opt = torch.optim.SGD(aux, lr=aux_lr, momentum=0.9)
     n_concord = sum(l.packed_w.numel() for l in layers)
-    n_aux = sum(p.numel() for p in aux_parameters(model))
-    log, t_train = [], 0.0
+    n_aux = sum(p.numel() for p in aux)
+    x = torch.zeros(batch, block, dtype=torch.long, device=device)
+    y = torch.zeros_like(x)
+    for p in aux:
+        p.grad = torch.zeros_like(p)
+
+    def step():
+        opt.zero_grad(set_to_none=False)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = model(x, y)
+        loss.backward()               # Concord layers step inside the backward
+        opt.step()
+        for l in layers:
+            l.rebalance()
+        return loss
+
+    g, static_loss, log, t_dev = None, None, [], []
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        log, t_dev, g = _chargpt_loop(steps, lr, warmup, layers, data, batch, block, x, y, graph, step, log_every)
+    torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in t_dev) / len(t_dev)
+    return dict(losses=log, steps_per_s=1e3 / ms, ms_per_step=ms, concord_params=n_concord, aux_params=n_aux,
+                entropy_floor=data.entropy_rate(), tokens_per_step=batch * block, cuda_graph=graph)
+
+
+def _chargpt_loop(steps, lr, warmup, layers, data, batch, block, x, y, graph, step, log_every):
+    g, static_loss, log, t_dev = None, None, [], []
     for it in range(steps):
         cur = lr_at(it, lr, warmup, steps)
         for l in layers:
             l.lr = cur
-        for grp in aux.param_groups:
-            grp["lr"] = lr_at(it, aux_lr, warmup, steps)
-        x, y = data.batch(batch, block)
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        with torch.autocast("cuda", dtype=torch.bfloat16):
-            loss = model(x, y)
-        loss.backward()               # Concord layers step inside the backward
-        aux.step()
-        aux.zero_grad(set_to_none=True)
-        for l in layers:
-            l.rebalance()
-        torch.cuda.synchronize()
+        xb, yb = data.batch(batch, block)
+        x.copy_(xb)
+        y.copy_(yb)
+        if graph and g is None and it == 10:
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                static_loss = step()
+            x.copy_(xb)
+            y.copy_(yb)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        if g is not None:
+            g.replay()
+            loss = static_loss
+        else:
+            loss = step()
+        e1.record()
         if it >= 10:
-            t_train += time.perf_counter() - t0
+            t_dev.append((e0, e1))
         if it % log_every == 0 or it == steps - 1:
             log.append((it, float(loss.item())))
-    return dict(losses=log, steps_per_s=(steps - 10) / t_train, concord_params=n_concord, aux_params=n_aux,
-                entropy_floor=data.entropy_rate(), tokens_per_step=batch * block)
+        if g is None:
+            del loss
+    return log, t_dev, g
+
+
+def run_steps(step_fn, refill, steps, warmup, layers, lr, graph, world=1, group=None):
+    """Run `warmup` eager steps, then `steps` timed ones.  With `graph` the
+    whole training step (forward, backward with the packed steps inside, the
+    other parameters' update, rebalance) is captured once as a CUDA graph and
+    replayed.  `refill(it)` writes the next batch into the step's static
+    inputs (outside the timed region).  Returns per-step device times (max over
+    ranks) and losses."""
+    import torch.distributed as dist
+    dev = torch.device("cuda", torch.cuda.current_device())
+    times, losses = [], []
+    g = None
+    static_loss = None
+    # every step, eager or captured, runs on one side stream: the parameters'
+    # AccumulateGrad nodes are created on the stream of the first backward,
+    # and a captured backward must not depend on the legacy default stream
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for it in range(warmup + steps):
+            for l in layers:              # linear lr warm-up over 100 steps, as the reference's trainers
+                l.lr = lr * min(1.0, (it + 1) / 100)
+            refill(it)
+            if graph and g is None and it == warmup:   # capture after the eager warm-up
+                torch.cuda.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    static_loss = step_fn()
+                refill(it)
+            if world > 1:
+                dist.barrier(group=group)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            if g is not None:
+                g.replay()
+                loss = static_loss
+            else:
+                loss = step_fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1)
+            if world > 1:
+                tt = torch.tensor([ms], device=dev)
+                dist.all_reduce(tt, op=dist.ReduceOp.MAX, group=group)
+                ms = float(tt.item())
+            if it >= warmup:
+                times.append(ms)
+            losses.append(float(loss.item()))
+            if g is None:
+                del loss                  # no autograd graph kept alive into the capture
+    torch.cuda.current_stream(dev).wait_stream(side)
+    return times, losses
+
+
+def allreduce_grads(params, flat, world, group=None):
+    """Average the ordinary parameters' gradients over the ranks (one bucket)."""
+    import torch.distributed as dist
+    off = 0
+    for p in params:
+        flat[off:off + p.numel()].copy_(p.grad.view(-1))
+        off += p.numel()
+    dist.all_reduce(flat, group=group)
+    flat.div_(world)
+    off = 0
+    for p in params:
+        p.grad.view(-1).copy_(flat[off:off + p.numel()])
+        off += p.numel()
 
 
 # ---------------------------------------------------------------- config 5: Llama-style decoder
@@ -224,7 +330,7 @@ class Llama(nn.Module):
 
 
 def train_llama_dp(steps, warmup, batch_per_gpu=8, seq=2048, lr=5e-4, aux_lr=0.01, seed=0, n_layer=24,
-                   group=None):
+                   group=None, graph=True):
     """Config 5: data-parallel training steps of the Llama-style decoder, one
     process per GPU (torch.distributed already initialised when world > 1).
 
@@ -252,42 +358,26 @@ def train_llama_dp(steps, warmup, batch_per_gpu=8, seq=2048, lr=5e-4, aux_lr=0.0
     opt = torch.optim.SGD(aux, lr=aux_lr, momentum=0.9)
     flat = torch.zeros(sum(p.numel() for p in aux), dtype=torch.float32, device=dev)
     g = torch.Generator(device=dev).manual_seed(seed * 1000 + rank)
-    times, losses = [], []
-    for it in range(warmup + steps):
-        x = torch.randint(0, 32000, (batch_per_gpu, seq + 1), generator=g, device=dev)
-        if world > 1:
-            dist.barrier(group=group)
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
+    x = torch.zeros(batch_per_gpu, seq + 1, dtype=torch.long, device=dev)
+
+    def refill(it):
+        x.copy_(torch.randint(0, 32000, (batch_per_gpu, seq + 1), generator=g, device=dev))
+
+    def step():
+        opt.zero_grad(set_to_none=False)
         with torch.autocast("cuda", dtype=torch.bfloat16):
             loss = model(x[:, :-1], x[:, 1:])
         loss.backward()                       # every Concord layer steps (its shard) here
         if world > 1:                         # the ordinary parameters: one bucketed all-reduce
-            off = 0
-            for p in aux:
-                flat[off:off + p.numel()].copy_(p.grad.view(-1))
-                off += p.numel()
-            dist.all_reduce(flat, group=group)
-            flat.div_(world)
-            off = 0
-            for p in aux:
-                p.grad.view(-1).copy_(flat[off:off + p.numel()])
-                off += p.numel()
+            allreduce_grads(aux, flat, world, group)
         opt.step()
-        opt.zero_grad(set_to_none=False)
         for l in layers:
             l.rebalance()
-        e1.record()
-        torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1)
-        if world > 1:
-            t = torch.tensor([ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
-            ms = float(t.item())
-        if it >= warmup:
-            times.append(ms)
-        losses.append(float(loss.item()))
+        return loss
+
+    for p in aux:                             # gradients accumulate into fixed buffers (graph replay)
+        p.grad = torch.zeros_like(p)
+    times, losses = run_steps(step, refill, steps, warmup, layers, lr, graph, world, group)
     for st in steppers:
         st.check()
     params = sum(l.packed_w.numel() for l in layers)
@@ -410,6 +500,14 @@ class SDXLUNet(nn.Module):
         self.norm_out = nn.GroupNorm(32, c0, eps=1e-5)
         self.conv_out = nn.Conv2d(c0, in_ch, 3, padding=1)
 
+    ckpt = False   # recompute each ResNet / transformer block in the backward
+
+    def _run(self, mod, *args):
+        if self.ckpt and torch.is_grad_enabled():
+            from torch.utils.checkpoint import checkpoint
+            return checkpoint(mod, *args, use_reentrant=False)
+        return mod(*args)
+
     def forward(self, x, t, ctx, pooled, time_ids):
         emb = self.time_lin2(F.silu(self.time_lin1(timestep_features(t, self.time_lin1.in_features))))
         tid = timestep_features(time_ids.reshape(-1), 256).reshape(x.shape[0], -1)
@@ -419,19 +517,19 @@ class SDXLUNet(nn.Module):
         skips = [h]
         for blk in self.down:
             for i, r in enumerate(blk.res):
-                h = r(h, emb)
+                h = self._run(r, h, emb)
                 if blk.attn is not None:
-                    h = blk.attn[i](h, ctx)
+                    h = self._run(blk.attn[i], h, ctx)
                 skips.append(h)
             if blk.downsample is not None:
                 h = blk.downsample(h)
                 skips.append(h)
-        h = self.mid_res2(self.mid_attn(self.mid_res1(h, emb), ctx), emb)
+        h = self._run(self.mid_res2, self._run(self.mid_attn, self._run(self.mid_res1, h, emb), ctx), emb)
         for blk in self.up:
             for i, r in enumerate(blk.res):
-                h = r(torch.cat([h, skips.pop().to(h.dtype)], dim=1), emb)
+                h = self._run(r, torch.cat([h, skips.pop().to(h.dtype)], dim=1), emb)
                 if blk.attn is not None:
-                    h = blk.attn[i](h, ctx)
+                    h = self._run(blk.attn[i], h, ctx)
             if blk.upsample is not None:
                 h = blk.upsample(F.interpolate(h, scale_factor=2.0, mode="nearest"))
         return self.conv_out(F.silu(self.norm_out(h)))
@@ -449,15 +547,17 @@ def sdxl_batch(B, gen, device, res=128):
     return lat, ctx, pooled, t, noise, ids
 
 
-def train_sdxl_dp(steps, warmup, batch_per_gpu=4, res=128, lr=5e-4, aux_lr=1e-3, seed=0, group=None,
-                  gate=True):
+def train_sdxl_dp(steps, warmup, batch_per_gpu=4, res=128, lr=5e-5, aux_lr=1e-4, seed=0, group=None,
+                  gate=True, ckpt=False, graph=True):
     """Config 4: epsilon-prediction MSE fine-tune steps of the SDXL-architecture
     UNet (~2.6 B parameters, random init), bf16 autocast, Concord on every
     Linear and every convolution (3x3 ones as their reshaped [O, I*9] weight),
     SGD (momentum 0.9) on norms and biases.  One process per GPU; with more
     than one rank every packed layer is data-parallel (RowShardedStep inside
     loss.backward()) and the other parameters' gradients are all-reduced.
-    Weak scaling: `batch_per_gpu` samples per GPU."""
+    Weak scaling: `batch_per_gpu` samples per GPU.  lr 5e-5 is the
+    reference's SDXL setting (notebook/src/sdxl_train.py:154); `ckpt` recomputes
+    every block in the backward (activation checkpointing)."""
     import torch.distributed as dist
     from concord_b200.convert import concordify
     world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -465,6 +565,7 @@ def train_sdxl_dp(steps, warmup, batch_per_gpu=4, res=128, lr=5e-4, aux_lr=1e-3,
     dev = torch.device("cuda", torch.cuda.current_device())
     torch.manual_seed(seed)
     model = SDXLUNet().to(dev)
+    model.ckpt = ckpt
     n_total = sum(p.numel() for p in model.parameters())
     layers = concordify(model, lr=lr, convs=True)
     if not gate:
@@ -481,45 +582,32 @@ def train_sdxl_dp(steps, warmup, batch_per_gpu=4, res=128, lr=5e-4, aux_lr=1e-3,
     torch.cuda.synchronize()
     base_mem = torch.cuda.memory_allocated()
     torch.cuda.reset_peak_memory_stats()
-    times, losses = [], []
-    for it in range(warmup + steps):
+    static = [t.clone() for t in sdxl_batch(batch_per_gpu, g, dev, res)]
+
+    def refill(it):
         lat, ctx, pooled, t, noise, ids = sdxl_batch(batch_per_gpu, g, dev, res)
         alpha_bar = torch.cos(t.float() / 1000 * math.pi / 2) ** 2
         noisy = alpha_bar.sqrt()[:, None, None, None] * lat + (1 - alpha_bar).sqrt()[:, None, None, None] * noise
-        if world > 1:
-            dist.barrier(group=group)
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
+        for dst, src in zip(static, (noisy, ctx, pooled, t, noise, ids)):
+            dst.copy_(src)
+
+    def step():
+        opt.zero_grad(set_to_none=False)
+        noisy, ctx, pooled, t, noise, ids = static
         with torch.autocast("cuda", dtype=torch.bfloat16):
             pred = model(noisy, t, ctx, pooled, ids)
         loss = F.mse_loss(pred.float(), noise)
         loss.backward()
         if world > 1:
-            off = 0
-            for p in aux:
-                flat[off:off + p.numel()].copy_(p.grad.view(-1))
-                off += p.numel()
-            dist.all_reduce(flat, group=group)
-            flat.div_(world)
-            off = 0
-            for p in aux:
-                p.grad.view(-1).copy_(flat[off:off + p.numel()])
-                off += p.numel()
+            allreduce_grads(aux, flat, world, group)
         opt.step()
-        opt.zero_grad(set_to_none=False)
         for l in layers:
             l.rebalance()
-        e1.record()
-        torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1)
-        if world > 1:
-            tt = torch.tensor([ms], device=dev)
-            dist.all_reduce(tt, op=dist.ReduceOp.MAX, group=group)
-            ms = float(tt.item())
-        if it >= warmup:
-            times.append(ms)
-        losses.append(float(loss.item()))
+        return loss
+
+    for p in aux:                             # gradients accumulate into fixed buffers (graph replay)
+        p.grad = torch.zeros_like(p)
+    times, losses = run_steps(step, refill, steps, warmup, layers, lr, graph, world, group)
     for st in steppers:
         st.check()
     out = dict(ms=times, losses=losses, params=n_total, concord_params=sum(l.packed_w.numel() for l in layers),
