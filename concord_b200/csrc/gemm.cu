@@ -15,9 +15,8 @@
 // reading TMEM with tcgen05.ld and storing through TMA.  A dW whose N x K
 // output has fewer tiles than the GPU has SMs splits its reduction into
 // slices (a batched GEMM into fp32 partials, summed in slice order and
-// rounded once to bf16).  Large outputs run the 2-SM form (256x256x64 tiles
-// on a CTA pair, cta_group::2, 2x1x1 cluster, plain non-multicast 2-SM TMA
-// loads); no load anywhere is multicast, so the kernels run in multi-GPU jobs.
+// rounded once to bf16).  Cluster shape 1x1x1:
+// every TMA load is a single-CTA load (the same kernels run in multi-GPU jobs).
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -95,43 +94,6 @@ using GemmDwSplitMain = typename cutlass::gemm::collective::CollectiveBuilder<
     cutlass::gemm::KernelTmaWarpSpecialized1SmSm100>::CollectiveOp;
 using GemmDwSplitKernel = cutlass::gemm::kernel::GemmUniversal<Shape<int, int, int, int>, GemmDwSplitMain, EpiF32, void>;
 using GemmDwSplit = cutlass::gemm::device::GemmUniversalAdapter<GemmDwSplitKernel>;
-
-// 2-SM form: one 256x256x64 MMA tile per CTA pair (tcgen05 cta_group::2) on a
-// static 2x1x1 cluster.  With that cluster CUTLASS's sm100 builder picks the
-// plain 2-SM TMA load for both operands (the pair splits the B tile; nothing
-// is multicast), so the kernels stay valid in multi-GPU jobs; operands are
-// always this GPU's own memory.
-using TileMNK2 = Shape<_256, _256, _64>;
-using Cluster2 = Shape<_2, _1, _1>;
-using Epi2 = typename cutlass::epilogue::collective::CollectiveBuilder<
-    cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, TileMNK2, Cluster2,
-    cutlass::epilogue::collective::EpilogueTileAuto, Acc, Acc, BF16, LayoutC, kAlign, BF16, LayoutC, kAlign,
-    cutlass::epilogue::TmaWarpSpecialized2Sm>::CollectiveOp;
-constexpr int kEpiSmem2 = static_cast<int>(sizeof(typename Epi2::SharedStorage));
-
-#define CONCORD_DEFINE_GEMM2(NAME, LA, LB)                                                                   \
-    using NAME##Main = typename cutlass::gemm::collective::CollectiveBuilder<                               \
-        cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, BF16, LA, kAlign, BF16, LB, kAlign, Acc,    \
-        TileMNK2, Cluster2, cutlass::gemm::collective::StageCountAutoCarveout<kEpiSmem2>,                   \
-        cutlass::gemm::KernelTmaWarpSpecialized2SmSm100>::CollectiveOp;                                    \
-    using NAME##Kernel = cutlass::gemm::kernel::GemmUniversal<Shape<int, int, int, int>, NAME##Main, Epi2, void>; \
-    using NAME = cutlass::gemm::device::GemmUniversalAdapter<NAME##Kernel>;
-
-CONCORD_DEFINE_GEMM2(GemmFwd2, cutlass::layout::RowMajor, cutlass::layout::ColumnMajor)
-CONCORD_DEFINE_GEMM2(GemmDx2, cutlass::layout::RowMajor, cutlass::layout::RowMajor)
-CONCORD_DEFINE_GEMM2(GemmDw2, cutlass::layout::ColumnMajor, cutlass::layout::RowMajor)
-
-// the 2-SM form for outputs with at least one full 256-row tile pair of work
-// per SM pair (CONCORD_GEMM_2SM=0 forces the 1-SM form)
-bool use_2sm(int64_t m, int64_t n) {
-    static const int mode = [] {
-        const char* e = getenv("CONCORD_GEMM_2SM");
-        return e ? atoi(e) : -1;
-    }();
-    if (mode == 0) return false;
-    if (mode == 1) return true;
-    return m >= 256 && n >= 256 && ((m + 255) / 256) * ((n + 255) / 256) >= 74;
-}
 
 // Slices for dW[N,K] over a reduction of M: only when the N x K output has
 // fewer 128x256 tiles than the GPU has SMs and each slice keeps >= 1024 rows
@@ -228,9 +190,6 @@ extern "C" int concord_gemm_fwd(const uint16_t* x, const uint16_t* w, uint16_t* 
                                 void* workspace, size_t workspace_bytes, void* stream) {
     if (bad(x) || bad(w) || bad(y)) return concord::fail(CONCORD_EALIGN, "concord_gemm_fwd: null or unaligned pointer");
     if (M <= 0 || N <= 0 || K <= 0) return concord::fail(CONCORD_ESHAPE, "concord_gemm_fwd: bad shape");
-    if (use_2sm(M, N))
-        return run_gemm<GemmFwd2>(x, w, y, (int)M, (int)N, (int)K, workspace, workspace_bytes,
-                                  reinterpret_cast<cudaStream_t>(stream), false, nullptr, "concord_gemm_fwd");
     return run_gemm<GemmFwd>(x, w, y, (int)M, (int)N, (int)K, workspace, workspace_bytes,
                              reinterpret_cast<cudaStream_t>(stream), false, nullptr, "concord_gemm_fwd");
 }
@@ -240,9 +199,6 @@ extern "C" int concord_gemm_dx(const uint16_t* dy, const uint16_t* w, uint16_t* 
                                void* workspace, size_t workspace_bytes, void* stream) {
     if (bad(dy) || bad(w) || bad(dx)) return concord::fail(CONCORD_EALIGN, "concord_gemm_dx: null or unaligned pointer");
     if (M <= 0 || N <= 0 || K <= 0) return concord::fail(CONCORD_ESHAPE, "concord_gemm_dx: bad shape");
-    if (use_2sm(M, K))
-        return run_gemm<GemmDx2>(dy, w, dx, (int)M, (int)K, (int)N, workspace, workspace_bytes,
-                                 reinterpret_cast<cudaStream_t>(stream), false, nullptr, "concord_gemm_dx");
     return run_gemm<GemmDx>(dy, w, dx, (int)M, (int)K, (int)N, workspace, workspace_bytes,
                             reinterpret_cast<cudaStream_t>(stream), false, nullptr, "concord_gemm_dx");
 }
@@ -253,9 +209,6 @@ extern "C" int concord_gemm_dw(const uint16_t* dy, const uint16_t* x, uint16_t* 
     if (bad(dy) || bad(x) || bad(dw)) return concord::fail(CONCORD_EALIGN, "concord_gemm_dw: null or unaligned pointer");
     if (M <= 0 || N <= 0 || K <= 0) return concord::fail(CONCORD_ESHAPE, "concord_gemm_dw: bad shape");
     const int S = dw_slices(M, N, K);
-    if (S == 1 && use_2sm(N, K))
-        return run_gemm<GemmDw2>(dy, x, dw, (int)N, (int)K, (int)M, workspace, workspace_bytes,
-                                 reinterpret_cast<cudaStream_t>(stream), false, nullptr, "concord_gemm_dw");
     if (S == 1)
         return run_gemm<GemmDw>(dy, x, dw, (int)N, (int)K, (int)M, workspace, workspace_bytes,
                                 reinterpret_cast<cudaStream_t>(stream), false, nullptr, "concord_gemm_dw");
@@ -282,13 +235,6 @@ extern "C" size_t concord_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) 
     run_gemm<GemmFwd>(nullptr, nullptr, nullptr, (int)M, (int)N, (int)K, nullptr, 0, nullptr, true, &a, "");
     run_gemm<GemmDx>(nullptr, nullptr, nullptr, (int)M, (int)K, (int)N, nullptr, 0, nullptr, true, &b, "");
     run_gemm<GemmDw>(nullptr, nullptr, nullptr, (int)N, (int)K, (int)M, nullptr, 0, nullptr, true, &c, "");
-    size_t a2 = 0, b2 = 0, c2 = 0;
-    run_gemm<GemmFwd2>(nullptr, nullptr, nullptr, (int)M, (int)N, (int)K, nullptr, 0, nullptr, true, &a2, "");
-    run_gemm<GemmDx2>(nullptr, nullptr, nullptr, (int)M, (int)K, (int)N, nullptr, 0, nullptr, true, &b2, "");
-    run_gemm<GemmDw2>(nullptr, nullptr, nullptr, (int)N, (int)K, (int)M, nullptr, 0, nullptr, true, &c2, "");
-    a = std::max(a, a2);
-    b = std::max(b, b2);
-    c = std::max(c, c2);
     const int S = dw_slices(M, N, K);
     if (S > 1) {
         size_t d = 0;
