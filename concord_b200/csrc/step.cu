@@ -585,34 +585,37 @@ __global__ void __launch_bounds__(STEP_THREADS, MINB) step_vec_kernel(StepArgs A
                 // argument; phase 2 the correctly rounded exp2(p*log2(x)) side by
                 // side; phase 3 the rest
 #pragma unroll
-                for (int h = 0; h < VEC; h += STEP_LOCK) {
-                    AdamwPre pre[STEP_LOCK];
-                    float xs[STEP_LOCK], den[STEP_LOCK];
-                    ElemOut o2[STEP_LOCK];
+                // the cheap reference-GPU arithmetic runs one element at a time
+                // (measured 1-2 % faster); the correctly rounded pow keeps pairs
+                constexpr int LK = (FL & FL_GPU) ? 1 : STEP_LOCK;
+                for (int h = 0; h < VEC; h += LK) {
+                    AdamwPre pre[LK];
+                    float xs[LK], den[LK];
+                    ElemOut o2[LK];
 #pragma unroll
-                    for (int u = 0; u < STEP_LOCK; ++u) {
+                    for (int u = 0; u < LK; ++u) {
                         const int j = h + u;
                         const float g = bf16_to_f32((gw[j >> 1] >> ((j & 1) * 16)) & 0xffffu);
                         pre[u] = adamw_pre<FL, true>(A.P, wv[j], g, rbits, cbits[j], vr, vc[j], cp[j], S);
                         xs[u] = pre[u].x;
                     }
 #pragma unroll
-                    for (int u = 0; u < STEP_LOCK; ++u) fixed_coh_divide<FL>(A.P, pre[u]);
+                    for (int u = 0; u < LK; ++u) fixed_coh_divide<FL>(A.P, pre[u]);
                     if (gpu_of<FL>(A.P)) {
 #pragma unroll
-                        for (int u = 0; u < STEP_LOCK; ++u)
+                        for (int u = 0; u < LK; ++u)
                             den[u] = div_full(pre[u].g, pow2log2_as(true, A.P.precond_p, xs[u]));
                     } else {
-                        crmath::cr_pow2log2<STEP_LOCK>(xs, A.P.precond_p, den);
+                        crmath::cr_pow2log2<LK>(xs, A.P.precond_p, den);
 #pragma unroll
-                        for (int u = 0; u < STEP_LOCK; ++u) den[u] = pre[u].g / den[u];
+                        for (int u = 0; u < LK; ++u) den[u] = pre[u].g / den[u];
                     }
-                    int32_t posv[STEP_LOCK];
+                    int32_t posv[LK];
 #pragma unroll
-                    for (int u = 0; u < STEP_LOCK; ++u) posv[u] = posn ^ (int32_t)(k0 + h + u);
-                    adamw_post_lockstep<FL, STEP_LOCK>(A.P, pre, den, S, posv, o2);
+                    for (int u = 0; u < LK; ++u) posv[u] = posn ^ (int32_t)(k0 + h + u);
+                    adamw_post_lockstep<FL, LK>(A.P, pre, den, S, posv, o2);
 #pragma unroll
-                    for (int u = 0; u < STEP_LOCK; ++u) outs[h + u] = o2[u];
+                    for (int u = 0; u < LK; ++u) outs[h + u] = o2[u];
                 }
             } else {
 #pragma unroll

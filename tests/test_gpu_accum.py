@@ -148,3 +148,49 @@ def test_sigmag_noise(pb, iso):
     finally:
         set_sigmag_noise(False)
         set_sigmag_sigma(0.0)
+
+
+@pytest.mark.parametrize("case", ["bare", "consol", "ratio", "wd"])
+def test_gate_matches_prototype_fixtures(pb, case):
+    """The CUDA gate against the reference's prototype kernel itself
+    (tests/golden/make_golden_accum.py), micro-step by micro-step."""
+    import ctypes
+    from concord_b200 import _abi
+    from test_oracle_accum import replay_accum_fixture
+    z = load("accum_" + case)
+    lib = _abi.load()
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(DEV)  # noqa: E731
+    rexp, cexp = dev(z["row_exp"]), dev(z["col_exp"])
+    vr, vc, svi = dev(z["v_row"]), dev(z["v_col"]), dev(z["sum_v_inv"])
+    flag_d = torch.zeros(1, dtype=torch.int32, device=DEV)
+    floors_d = torch.zeros(2, dtype=torch.float32, device=DEV)
+    lr_d, eps_d, salt_d = (torch.zeros(1, device=DEV), torch.zeros(1, device=DEV),
+                           torch.zeros(1, dtype=torch.int32, device=DEV))
+    p = lambda t: None if t is None else ctypes.c_void_p(t.data_ptr())  # noqa: E731
+
+    def step(P, flag, floors, packed, grad, wbuf, rm, cm, coh, lr, eps, salt):
+        flag_d.fill_(int(flag[0]))
+        P.consolidate = flag_d.data_ptr()
+        if floors is not None:
+            floors_d.copy_(torch.from_numpy(floors))
+            P.ratio_floors = floors_d.data_ptr()
+        lr_d.fill_(lr)
+        eps_d.fill_(eps)
+        salt_d.fill_(salt)
+        pk, w = dev(packed), dev(wbuf.view(np.int16))
+        g = dev(grad.view(np.int16))
+        rmd, cmd = dev(rm), dev(cm)
+        cd = dev(coh) if coh is not None else None
+        N, K = packed.shape
+        rc = lib.concord_step(ctypes.byref(P), p(pk), K, p(g), K, p(w), K, p(rexp), p(cexp), p(rmd), p(cmd),
+                              p(vr), p(vc), p(svi), p(cd), K, p(lr_d), p(eps_d), p(salt_d), N, K, 0, None,
+                              ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        assert rc == 0, lib.concord_last_error()
+        torch.cuda.synchronize()
+        packed[...] = pk.cpu().numpy()
+        wbuf[...] = w.cpu().numpy().view(np.uint16)
+        rm[...] = rmd.cpu().numpy()
+        cm[...] = cmd.cpu().numpy()
+        if coh is not None:
+            coh[...] = cd.cpu().numpy()
+    assert replay_accum_fixture(z, step) == []

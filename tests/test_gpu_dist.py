@@ -66,7 +66,9 @@ def _worker(rank, world, port, out_dir, N, transport, via_backward=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world)
+    from concord_b200 import packed_b
     from concord_b200.distributed import RowShardedStep
+    packed_b.set_arithmetic("cr")        # the same arithmetic as the emulation in the test process
     dev = torch.device("cuda", rank)
     layer = _layer(N, dev)
     st = RowShardedStep(layer, transport=transport)

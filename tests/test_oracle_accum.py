@@ -42,3 +42,48 @@ def test_consolidate_one_is_the_plain_step(oracle_mod):
     b = _case(oracle_mod, None)
     for x, y in zip(a, b):
         assert np.array_equal(x, y)
+
+
+ACCUM_CASES = ["bare", "consol", "ratio", "wd"]
+
+
+def replay_accum_fixture(z, step_fn):
+    """Drive `step_fn(P, packed, grad, wbuf, rmax, cmax, coh, lr, eps, salt)` through
+    a prototype fixture's micro-step sequence; returns the per-step mismatches."""
+    from golden_util import lr_eps, params_of
+    P = params_of(z)
+    lr, eps = lr_eps(z)
+    N, K = int(z["N"]), int(z["K"])
+    flag = np.zeros(1, np.int32)
+    floors = np.array([z["cfg_chase_floor"], z["cfg_leak_floor"]], np.float32)
+    packed = z["init_packed"].copy()
+    coh = z["init_coh_pre"].copy() if z["init_coh_pre"].size else None
+    wbuf = np.full((N, K), 7, np.uint16)
+    bad = []
+    for t, cons in enumerate(z["consolidate"]):
+        flag[0] = cons
+        rm, cm = np.zeros(N, np.int32), np.zeros(K, np.int32)
+        step_fn(P, flag, floors if bool(z["cfg_ratio"]) else None, packed, z[f"grad{t}"], wbuf, rm, cm, coh,
+                lr, eps, int(z[f"salt{t}"]))
+        for name, got in (("packed", packed), ("wbuf", wbuf), ("rmax", rm), ("cmax", cm)) + \
+                (((("coh_pre", coh),)) if coh is not None else ()):
+            if not np.array_equal(got, z[f"{name}{t}"]):
+                bad.append((t, name, int((got != z[f"{name}{t}"]).sum())))
+    return bad
+
+
+def test_oracle_matches_prototype_accumulation_fixtures(oracle_mod):
+    """The gate pinned to the reference's prototype kernel itself
+    (tests/golden/make_golden_accum.py): tick-only micro-steps and
+    consolidating steps, bit for bit."""
+    from golden_util import load
+
+    for case in ACCUM_CASES:
+        z = load("accum_" + case)
+
+        def step(P, flag, floors, packed, grad, wbuf, rm, cm, coh, lr, eps, salt):
+            P.consolidate = flag.ctypes.data
+            P.ratio_floors = floors.ctypes.data if floors is not None else None
+            oracle_mod.step(P, packed, grad, wbuf, z["row_exp"], z["col_exp"], rm, cm, z["v_row"].copy(),
+                            z["v_col"].copy(), z["sum_v_inv"].copy(), coh, lr, eps, salt)
+        assert replay_accum_fixture(z, step) == [], case
