@@ -140,3 +140,36 @@ def export_dense(model, dtype=torch.bfloat16):
         parent, _, leaf = name.rpartition(".")
         setattr(out.get_submodule(parent) if parent else out, leaf, dense)
     return out
+
+
+@torch.no_grad()
+def dense_state_dict(model, dtype=torch.bfloat16):
+    """The state_dict of export_dense(model) without copying the model: every
+    packed layer contributes `<name>.weight` (its consolidated_weight(), 4-D for
+    convolutions) and `<name>.bias`, in `dtype`; every other parameter and
+    buffer is taken as it is."""
+    packed = dict(packed_layers(model))
+    out = {}
+    for name, m in packed.items():
+        pre = name + "." if name else ""
+        w = m.consolidated_weight().to(dtype)
+        if isinstance(m, _pb.ConcordConv2dPackedB):
+            w = w.view(m.out_channels, m.in_channels, m.kh, m.kw)
+        out[pre + "weight"] = w
+        if getattr(m, "bias", None) is not None:
+            out[pre + "bias"] = m.bias.detach().to(dtype)
+    for k, v in model.state_dict().items():
+        if k.rpartition(".")[0] in packed:      # a packed layer's own buffers
+            continue
+        out[k] = v.detach()
+    return out
+
+
+def save_consolidated(model, path, dtype=torch.bfloat16):
+    """Write the deployable dense weights as a safetensors file (the
+    reference's final save: packed layers consolidated back to plain
+    Linear / Conv2d weights, so the checkpoint loads as the ordinary model)."""
+    from safetensors.torch import save_file
+    sd = {k: v.contiguous().cpu() for k, v in dense_state_dict(model, dtype).items()}
+    save_file(sd, path)
+    return sorted(sd)

@@ -107,3 +107,26 @@ def test_export_dense_matches_the_consolidated_weight():
     assert isinstance(dc, torch.nn.Conv2d) and dc.padding == (1, 1)
     assert torch.equal(dc.weight.view(torch.int16),
                        conv.consolidated_weight().view(8, 4, 3, 3).view(torch.int16))
+
+
+def test_consolidated_safetensors_export(tmp_path):
+    """The final save: a safetensors file of plain Linear / Conv2d weights equal to
+    export_dense(model)'s state_dict, loadable into the dense model."""
+    import torch.nn as nn
+    from safetensors.torch import load_file
+    from concord_b200 import ConcordConv2dPackedB, ConcordLinearPackedB
+    from concord_b200.checkpoint import export_dense, save_consolidated
+    torch.manual_seed(0)
+    model = nn.Sequential(ConcordLinearPackedB(64, 48, bias=True, device="cuda"), nn.LayerNorm(48),
+                          ConcordLinearPackedB(48, 32, bias=False, device="cuda")).cuda()
+    conv = ConcordConv2dPackedB(8, 16, 3, padding=1, device="cuda")
+    model.add_module("conv", conv)
+    x = torch.randn(16, 64, device="cuda", requires_grad=True)
+    model[2](model[1](model[0](x))).float().pow(2).mean().backward()
+    path = str(tmp_path / "dense.safetensors")
+    keys = save_consolidated(model, path)
+    got = load_file(path)
+    want = export_dense(model).state_dict()
+    assert sorted(want) == keys
+    for k, v in want.items():
+        assert torch.equal(got[k], v.detach().cpu().to(got[k].dtype)), k
