@@ -161,6 +161,13 @@ int run_gemm(const void* A, const void* B, void* D, int M, int N, int K, void* w
         return e ? atoi(e) : 1;
     }();
     args.scheduler.max_swizzle_size = swz;
+    // raster order of the output tiles: 0 CUTLASS's heuristic, 1 along M, 2 along N
+    static const int raster = [] {
+        const char* e = getenv("CONCORD_GEMM_RASTER");
+        return e ? atoi(e) : 0;
+    }();
+    using RO = decltype(args.scheduler.raster_order);
+    args.scheduler.raster_order = raster == 1 ? RO::AlongM : raster == 2 ? RO::AlongN : RO::Heuristic;
     Gemm gemm;
     if (query_only) {
         *ws_needed = Gemm::get_workspace_size(args);
