@@ -160,7 +160,7 @@ def backward_time(n_rows, k_cols, device, iters=20):
 
 
 SHARDED = None
-STEP_TRAFFIC_PER_PARAM = (84.000768e6 + 55.366656e6) / (4096 * 2048)
+STEP_TRAFFIC_PER_PARAM = (83.988224e6 + 29.4656e6) / (4096 * 2048)
 
 
 def optimizer_step(layer, grad, coh_stats=None, ev=None):
