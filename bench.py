@@ -678,11 +678,17 @@ def main():
     })
     if world == 1:
         bms, fms = backward_time(args.rows, args.cols, device)
+        packed_b.set_fused_dw_vhat(False)
+        bms_sep, _ = backward_time(args.rows, args.cols, device)
+        packed_b.set_fused_dw_vhat(True)
         d["backward"] = {"ms": bms, "forward_ms": fms, "tokens": M,
                          "gemm_tflops": 2 * 2.0 * M * args.rows * args.cols / (bms * 1e-3) / 1e12,
                          "packed_path_share": ms_share(r["ms"], bms),
-                         "note": "loss.backward() of one bare layer through the drop-in API: dX and dW "
-                                 "GEMMs + v-hat + packed step, then rebalance(); CUDA events, eager"}
+                         "ms_vhat_separate": bms_sep,
+                         "note": "loss.backward() of one bare layer through the drop-in API: dX GEMM, "
+                                 "dW GEMM with the v-hat partials in its epilogue + v-hat fold, packed step, "
+                                 "then rebalance(); CUDA events, eager.  ms_vhat_separate: the same with "
+                                 "the dW GEMM and a standalone v-hat launch"}
     if not args.no_cpu_baseline:
         v1, dt = cpu_baseline(rows=2048, threads=1)
         port = {"value": v1, "unit": "GB/s", "cores": 1, "kind": "port",

@@ -196,6 +196,9 @@ _SIGS = [
     ("concord_gemm_fwd", ctypes.c_int, [_P, _P, _P, _I64, _I64, _I64, _P, ctypes.c_size_t, _P]),
     ("concord_gemm_dx", ctypes.c_int, [_P, _P, _P, _I64, _I64, _I64, _P, ctypes.c_size_t, _P]),
     ("concord_gemm_dw", ctypes.c_int, [_P, _P, _P, _I64, _I64, _I64, _P, ctypes.c_size_t, _P]),
+    ("concord_gemm_dw_vhat_workspace_bytes", ctypes.c_size_t, [_I64, _I64, _I64]),
+    ("concord_gemm_dw_vhat", ctypes.c_int,
+     [_P, _P, _P, _I64, _I64, _I64, _P, _P, _P, _F, _F, _P, _P, _P, _P, ctypes.c_size_t, _P]),
     ("concord_im2col", ctypes.c_int,
      [_P, _I64, _I64, _I64, _I64, _I32, _I32, _I32, _I32, _I32, _I32, _P, _P]),
     ("concord_col2im", ctypes.c_int,

@@ -36,6 +36,9 @@
 
 namespace concord {
 int fail(int code, const std::string& msg);
+int vhat_fold_partials(const float* rp, int64_t ldrp, const float* cp, int64_t ldcp, int64_t N, int64_t K,
+                       float* v_row, float* v_col, float* sum_v_inv, float beta2, float one_minus_beta2,
+                       int32_t* row_max, int32_t* col_max, int32_t* salt, unsigned* cnt, cudaStream_t st);
 
 __global__ void splitk_reduce_kernel(const float4* __restrict__ part, uint2* __restrict__ out, int64_t n4, int S) {
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
@@ -94,6 +97,75 @@ using GemmDwSplitMain = typename cutlass::gemm::collective::CollectiveBuilder<
     cutlass::gemm::KernelTmaWarpSpecialized1SmSm100>::CollectiveOp;
 using GemmDwSplitKernel = cutlass::gemm::kernel::GemmUniversal<Shape<int, int, int, int>, GemmDwSplitMain, EpiF32, void>;
 using GemmDwSplit = cutlass::gemm::device::GemmUniversalAdapter<GemmDwSplitKernel>;
+
+// dW with the v-hat partials in its epilogue.  The epilogue visitor tree
+// (CUTLASS's sm90/sm100 EVT nodes) computes, per output element,
+// v = float(bf16_rn(acc)) -- the stored dW value itself -- and s = v * v,
+// stores bf16(v) (exact: v is already a bf16 value) as dW, and reduces s per
+// 128 x 256 output tile into two fixed-order partial arrays in the workspace:
+//   ColReduction (sum over the tile's 256 columns): row partial rp[slab][n]
+//   RowReduction (sum over the tile's 128 rows):   column partial cp[rblk][k]
+// (non-final reductions: each tile writes its own partial, no atomics), the
+// same tiling and partial layout as vhat_kernel's tiles, so vhat's
+// fixed-order fold turns them into v_row / v_col / sum_v_inv.  The
+// in-tile summation order is CUTLASS's (register, then warp-shuffle, then
+// shared-memory tree), deterministic but not vhat_kernel's order: the
+// v-hat it yields agrees with the standalone kernel's to fp32 rounding, and
+// the dW it stores is bit-identical to concord_gemm_dw's.
+namespace vhfuse {
+using namespace cutlass::epilogue::fusion;
+constexpr auto RN = cutlass::FloatRoundStyle::round_to_nearest;
+
+template <class T>
+struct RoundBf16 {
+    template <int N>
+    CUTLASS_DEVICE cutlass::Array<float, N> operator()(cutlass::Array<float, N> const& a) const {
+        cutlass::Array<float, N> r;
+        CUTLASS_PRAGMA_UNROLL
+        for (int i = 0; i < N; ++i) r[i] = __bfloat162float(__float2bfloat16_rn(a[i]));
+        return r;
+    }
+};
+template <class T>
+struct SquareRn {   // one rounding per square: never contracted into the sum
+    template <int N>
+    CUTLASS_DEVICE cutlass::Array<float, N> operator()(cutlass::Array<float, N> const& a) const {
+        cutlass::Array<float, N> r;
+        CUTLASS_PRAGMA_UNROLL
+        for (int i = 0; i < N; ++i) r[i] = __fmul_rn(a[i], a[i]);
+        return r;
+    }
+};
+template <class T>
+struct TakeFirst {
+    template <int N>
+    CUTLASS_DEVICE cutlass::Array<float, N> operator()(cutlass::Array<float, N> const& a,
+                                                       cutlass::Array<float, N> const&) const {
+        return a;
+    }
+};
+
+using Val = Sm90EVT<Sm90Compute<RoundBf16, float, float, RN>, Sm90AccFetch>;
+using Sq = Sm90EVT<Sm90Compute<SquareRn, float, float, RN>, Val>;
+using RowPart = Sm90ColReduction<cutlass::plus, cutlass::plus, cutlass::plus, 0, TileMNK, float, float, RN,
+                                 Stride<_1, _0, _0>, 4, true, false, true>;
+using ColPart = Sm90RowReduction<cutlass::plus, cutlass::plus, cutlass::plus, 0, TileMNK, float, float, RN,
+                                 Stride<_0, _1, _0>, 4, true, false, true>;
+using Parts = Sm90EVT<ColPart, Sm90EVT<RowPart, Sq>>;
+using Root = Sm90EVT<Sm90Compute<TakeFirst, cutlass::bfloat16_t, float, RN>, Val, Parts>;   // dW out as bf16
+}  // namespace vhfuse
+
+using EpiVhat = typename cutlass::epilogue::collective::CollectiveBuilder<
+    cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, TileMNK, Cluster,
+    cutlass::epilogue::collective::EpilogueTileAuto, Acc, Acc, void, LayoutC, kAlign, BF16, LayoutC, kAlign,
+    cutlass::epilogue::TmaWarpSpecialized1Sm, vhfuse::Root>::CollectiveOp;
+using GemmDwVhatMain = typename cutlass::gemm::collective::CollectiveBuilder<
+    cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, BF16, cutlass::layout::ColumnMajor, kAlign, BF16,
+    cutlass::layout::RowMajor, kAlign, Acc, TileMNK, Cluster,
+    cutlass::gemm::collective::StageCountAutoCarveout<static_cast<int>(sizeof(typename EpiVhat::SharedStorage))>,
+    cutlass::gemm::KernelTmaWarpSpecialized1SmSm100>::CollectiveOp;
+using GemmDwVhatKernel = cutlass::gemm::kernel::GemmUniversal<Shape<int, int, int, int>, GemmDwVhatMain, EpiVhat, void>;
+using GemmDwVhat = cutlass::gemm::device::GemmUniversalAdapter<GemmDwVhatKernel>;
 
 // Slices for dW[N,K] over a reduction of M: only when the N x K output has
 // fewer 128x256 tiles than the GPU has SMs and each slice keeps >= 1024 rows
@@ -188,6 +260,56 @@ int run_gemm(const void* A, const void* B, void* D, int M, int N, int K, void* w
     return CONCORD_OK;
 }
 
+// dW[N,K] = DY^T X with the v-hat partials (GEMM m=N, n=K, k=M): rp receives
+// [ceil(K/256)][round_up(N,128)] row partials, cp [ceil(N/128)][round_up(K,256)]
+// column partials (fp32 sums of the squared bf16 outputs per tile)
+int run_gemm_dw_vhat(const void* dy, const void* x, void* dw, int N, int K, int M, float* rp, float* cp,
+                     void* workspace, size_t ws_bytes, cudaStream_t stream, bool query_only, size_t* ws_needed) {
+    using Gemm = GemmDwVhat;
+    using StrideA = typename Gemm::GemmKernel::StrideA;
+    using StrideB = typename Gemm::GemmKernel::StrideB;
+    using StrideC = typename Gemm::GemmKernel::StrideC;
+    using StrideD = typename Gemm::GemmKernel::StrideD;
+    StrideA sa = cutlass::make_cute_packed_stride(StrideA{}, cute::make_shape(N, M, 1));
+    StrideB sb = cutlass::make_cute_packed_stride(StrideB{}, cute::make_shape(K, M, 1));
+    StrideC sc = cutlass::make_cute_packed_stride(StrideC{}, cute::make_shape(N, K, 1));
+    StrideD sd = cutlass::make_cute_packed_stride(StrideD{}, cute::make_shape(N, K, 1));
+    using RowPartArgs = typename vhfuse::RowPart::Arguments;
+    using ColPartArgs = typename vhfuse::ColPart::Arguments;
+    typename Gemm::Arguments args{
+        cutlass::gemm::GemmUniversalMode::kGemm,
+        {N, K, M, 1},
+        {reinterpret_cast<const BF16*>(dy), sa, reinterpret_cast<const BF16*>(x), sb},
+        {{{{}, {}},                                                         // v = bf16(acc)
+          {{{{{}, {}}, {}}, RowPartArgs{rp, 0.0f, {}}}, ColPartArgs{cp, 0.0f, {}}},  // partials of v*v
+          {}},
+         nullptr, sc, reinterpret_cast<BF16*>(dw), sd}};
+    static const int swz = [] {
+        const char* e = getenv("CONCORD_GEMM_SWIZZLE");
+        return e ? atoi(e) : 1;
+    }();
+    args.scheduler.max_swizzle_size = swz;
+    Gemm gemm;
+    if (query_only) {
+        *ws_needed = Gemm::get_workspace_size(args);
+        return CONCORD_OK;
+    }
+    const char* name = "concord_gemm_dw_vhat";
+    if (gemm.can_implement(args) != cutlass::Status::kSuccess)
+        return concord::fail(CONCORD_ESHAPE, std::string(name) + ": shape/alignment not supported "
+                                             "(every extent must be a multiple of 8)");
+    if (Gemm::get_workspace_size(args) > ws_bytes)
+        return concord::fail(CONCORD_EWORKSPACE, std::string(name) + ": workspace too small");
+    if (int rc = bind_current_context(name)) return rc;
+    if (gemm.initialize(args, workspace, stream) != cutlass::Status::kSuccess)
+        return concord::fail(CONCORD_ELAUNCH, std::string(name) + ": initialize failed");
+    if (gemm.run(stream) != cutlass::Status::kSuccess)
+        return concord::fail(CONCORD_ELAUNCH, std::string(name) + ": launch failed");
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return concord::fail(CONCORD_ELAUNCH, std::string(name) + ": " + cudaGetErrorString(e));
+    return CONCORD_OK;
+}
+
 bool bad(const void* p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) % 16) != 0; }
 
 }  // namespace
@@ -250,4 +372,75 @@ extern "C" size_t concord_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) 
         c = std::max(c, (size_t)S * (size_t)N * (size_t)K * sizeof(float) + d);
     }
     return std::max(a, std::max(b, c));
+}
+
+// ---- dW with the v-hat update (the partials in the dW epilogue) ----
+namespace {
+struct DwVhatLayout {
+    int64_t ldrp, ldcp;      // partial strides: N and K rounded up to the tile
+    size_t off_rp, off_cp, off_gemm, total;
+};
+DwVhatLayout dw_vhat_layout(int64_t M, int64_t N, int64_t K) {
+    DwVhatLayout L;
+    const int64_t ncs = (K + 255) / 256, nrb = (N + 127) / 128;
+    L.ldrp = nrb * 128;
+    L.ldcp = ncs * 256;
+    L.off_rp = 256;   // the fold's arrival counter first
+    L.off_cp = L.off_rp + ((size_t)ncs * (size_t)L.ldrp * sizeof(float) + 255) / 256 * 256;
+    L.off_gemm = L.off_cp + ((size_t)nrb * (size_t)L.ldcp * sizeof(float) + 255) / 256 * 256;
+    size_t g = 0;
+    run_gemm_dw_vhat(nullptr, nullptr, nullptr, (int)N, (int)K, (int)M, nullptr, nullptr, nullptr, 0, nullptr, true, &g);
+    L.total = L.off_gemm + g;
+    return L;
+}
+}  // namespace
+
+// the epilogue form runs where the dW GEMM fills the GPU with whole output
+// tiles (>= 148 tiles of 128 x 256, never split); smaller layers take the
+// two-launch path, whose v-hat order the CPU oracle restates
+bool dw_vhat_fused(int64_t M, int64_t N, int64_t K) {
+    return ((N + 127) / 128) * ((K + 255) / 256) >= 148 && dw_slices(M, N, K) == 1;
+}
+
+extern "C" size_t concord_gemm_dw_vhat_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+    if (M <= 0 || N <= 0 || K <= 0) return 0;
+    if (!dw_vhat_fused(M, N, K)) {
+        const size_t v = (concord_vhat_workspace_bytes(N, K) + 255) / 256 * 256;
+        return v + concord_gemm_workspace_bytes(M, N, K);
+    }
+    return dw_vhat_layout(M, N, K).total;
+}
+
+// dW = DY^T X (bf16, as concord_gemm_dw) followed by the v-hat update of
+// concord_vhat_update on it.  On a layer of >= 148 output tiles the squares'
+// tile partials come out of the GEMM's epilogue and one fold launch
+// finishes; smaller layers run concord_gemm_dw then concord_vhat_update.
+extern "C" int concord_gemm_dw_vhat(const uint16_t* dy, const uint16_t* x, uint16_t* dw, int64_t M, int64_t N,
+                                    int64_t K, float* v_row, float* v_col, float* sum_v_inv, float beta2,
+                                    float one_minus_beta2, int32_t* row_max, int32_t* col_max, int32_t* salt,
+                                    void* workspace, size_t workspace_bytes, void* stream) {
+    const char* name = "concord_gemm_dw_vhat";
+    if (bad(dy) || bad(x) || bad(dw) || bad(workspace))
+        return concord::fail(CONCORD_EALIGN, std::string(name) + ": null or unaligned pointer");
+    if (!v_row || !v_col || !sum_v_inv) return concord::fail(CONCORD_EINVAL, std::string(name) + ": null v-hat pointer");
+    if (M <= 0 || N <= 0 || K <= 0) return concord::fail(CONCORD_ESHAPE, std::string(name) + ": bad shape");
+    if (workspace_bytes < concord_gemm_dw_vhat_workspace_bytes(M, N, K))
+        return concord::fail(CONCORD_EWORKSPACE, std::string(name) + ": workspace smaller than "
+                                                 "concord_gemm_dw_vhat_workspace_bytes(M, N, K)");
+    char* ws = static_cast<char*>(workspace);
+    if (!dw_vhat_fused(M, N, K)) {
+        const size_t v = (concord_vhat_workspace_bytes(N, K) + 255) / 256 * 256;
+        if (int rc = concord_gemm_dw(dy, x, dw, M, N, K, ws + v, workspace_bytes - v, stream)) return rc;
+        return concord_vhat_update(dw, K, N, K, v_row, v_col, sum_v_inv, beta2, one_minus_beta2, row_max, col_max,
+                                   salt, ws, v, stream);
+    }
+    const DwVhatLayout L = dw_vhat_layout(M, N, K);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    float* rp = reinterpret_cast<float*>(ws + L.off_rp);
+    float* cp = reinterpret_cast<float*>(ws + L.off_cp);
+    if (int rc = run_gemm_dw_vhat(dy, x, dw, (int)N, (int)K, (int)M, rp, cp, ws + L.off_gemm,
+                                  workspace_bytes - L.off_gemm, st, false, nullptr))
+        return rc;
+    return concord::vhat_fold_partials(rp, L.ldrp, cp, L.ldcp, N, K, v_row, v_col, sum_v_inv, beta2,
+                                       one_minus_beta2, row_max, col_max, salt, reinterpret_cast<unsigned*>(ws), st);
 }

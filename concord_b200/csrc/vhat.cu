@@ -48,6 +48,10 @@ struct VhatArgs {
     const uint16_t* recv;
     int64_t S;
     PeerSync sync;
+    // fold only: partial strides (0: N for rp, K for cp), and whether the
+    // fold zeroes row_max/col_max and bumps the salt (partials made elsewhere)
+    int64_t ldrp, ldcp;
+    bool fold_resets;
 };
 
 // rows of a warp whose loads go out together: 8 for a local gradient, fewer
@@ -218,8 +222,11 @@ __global__ void __launch_bounds__(VH_THREADS) vhat_fold_kernel(VhatArgs A, int n
     __shared__ float red[VH_THREADS];
     __shared__ int last;
     if (err && ld_volatile(err) != 0) return;   // the partials were not written
+    const int64_t ldrp = A.ldrp ? A.ldrp : A.N, ldcp = A.ldcp ? A.ldcp : A.K;
     if ((int)blockIdx.x < ncb) {
         const int64_t col = (int64_t)blockIdx.x * VH_THREADS + threadIdx.x;
+        if (A.fold_resets && A.col_max && col < A.K) A.col_max[col] = 0;
+        if (A.fold_resets && A.salt && blockIdx.x == 0 && threadIdx.x == 0) *A.salt += 1;
         if (col < A.K) {
             // fixed order b = 0, 1, ..., nrb-1; the loads of 32 partials go out together
             float t = __ldcg(A.cp + col);
@@ -227,18 +234,18 @@ __global__ void __launch_bounds__(VH_THREADS) vhat_fold_kernel(VhatArgs A, int n
             for (; b + 32 <= A.nrb; b += 32) {
                 float v[32];
 #pragma unroll
-                for (int u = 0; u < 32; ++u) v[u] = __ldcg(A.cp + (int64_t)(b + u) * A.K + col);
+                for (int u = 0; u < 32; ++u) v[u] = __ldcg(A.cp + (int64_t)(b + u) * ldcp + col);
 #pragma unroll
                 for (int u = 0; u < 32; ++u) t = t + v[u];
             }
             for (; b + 8 <= A.nrb; b += 8) {
                 float v[8];
 #pragma unroll
-                for (int u = 0; u < 8; ++u) v[u] = __ldcg(A.cp + (int64_t)(b + u) * A.K + col);
+                for (int u = 0; u < 8; ++u) v[u] = __ldcg(A.cp + (int64_t)(b + u) * ldcp + col);
 #pragma unroll
                 for (int u = 0; u < 8; ++u) t = t + v[u];
             }
-            for (; b < A.nrb; ++b) t = t + __ldcg(A.cp + (int64_t)b * A.K + col);
+            for (; b < A.nrb; ++b) t = t + __ldcg(A.cp + (int64_t)b * ldcp + col);
             if (A.col_sum_out) A.col_sum_out[col] = t;
             else A.v_col[col] = A.b2 * A.v_col[col] + A.omb2 * t;
         }
@@ -246,9 +253,10 @@ __global__ void __launch_bounds__(VH_THREADS) vhat_fold_kernel(VhatArgs A, int n
     }
     const int nrf = (int)gridDim.x - ncb;
     const int64_t n = (int64_t)(blockIdx.x - ncb) * VH_THREADS + threadIdx.x;
+    if (A.fold_resets && A.row_max && n < A.N) A.row_max[n] = 0;
     if (n < A.N) {
         float t = __ldcg(A.rp + n);
-        for (int c = 1; c < A.ncs; ++c) t = t + __ldcg(A.rp + (int64_t)c * A.N + n);
+        for (int c = 1; c < A.ncs; ++c) t = t + __ldcg(A.rp + (int64_t)c * ldrp + n);
         A.v_row[n] = A.b2 * A.v_row[n] + A.omb2 * t;
     }
     __syncthreads();
@@ -298,6 +306,26 @@ static void vhat_fold(const VhatArgs& A, const int32_t* err, cudaStream_t st) {
     const int ncb = (int)((A.K + VH_THREADS - 1) / VH_THREADS);
     const int64_t nrf = A.N > 0 ? (A.N + VH_THREADS - 1) / VH_THREADS : 1;
     vhat_fold_kernel<<<(unsigned)(ncb + nrf), VH_THREADS, 0, st>>>(A, ncb, err);
+}
+
+// The fold of partials made elsewhere (the dW GEMM's epilogue): rp
+// [ceil(K/256)][ldrp], cp [ceil(N/128)][ldcp], cnt one zeroed counter that
+// the fold leaves zeroed; also zeroes row_max/col_max and bumps the salt.
+int vhat_fold_partials(const float* rp, int64_t ldrp, const float* cp, int64_t ldcp, int64_t N, int64_t K,
+                       float* v_row, float* v_col, float* sum_v_inv, float beta2, float one_minus_beta2,
+                       int32_t* row_max, int32_t* col_max, int32_t* salt, unsigned* cnt, cudaStream_t st) {
+    VhatArgs A{};
+    A.N = N; A.K = K;
+    A.v_row = v_row; A.v_col = v_col; A.sum_v_inv = sum_v_inv;
+    A.b2 = beta2; A.omb2 = one_minus_beta2;
+    A.row_max = row_max; A.col_max = col_max; A.salt = salt;
+    A.rp = const_cast<float*>(rp); A.cp = const_cast<float*>(cp); A.cnt = cnt;
+    A.ncs = (int)((K + VH_COLS - 1) / VH_COLS);
+    A.nrb = (int)((N + VH_ROWS - 1) / VH_ROWS);
+    A.ldrp = ldrp; A.ldcp = ldcp;
+    A.fold_resets = true;
+    vhat_fold(A, nullptr, st);
+    return check_launch("vhat_fold_partials");
 }
 
 // shard mode, after the all-reduce of (column sums, v_row sum) over ranks
@@ -393,7 +421,9 @@ extern "C" int concord_peer_reduce_vhat(const uint16_t* own_rows, const uint16_t
                                         float* col_sum_out, float* vsum_out, void* workspace,
                                         size_t workspace_bytes, const concord_peer_sync* sync, void* stream) {
     const char* name = "concord_peer_reduce_vhat";
-    if ((n_rows > 0 && (!own_rows || !recv)) || !grad_out || !v_row || !col_sum_out || !vsum_out || !sync || !sync->flags ||
+    // a rank without rows (more ranks than rows) passes empty own_rows /
+    // grad_out / v_row views, which may be null
+    if ((n_rows > 0 && (!own_rows || !recv || !grad_out || !v_row)) || !col_sum_out || !vsum_out || !sync || !sync->flags ||
         !sync->peer_flags || !sync->state)
         return fail(CONCORD_EINVAL, std::string(name) + ": null pointer");
     if (sync->n_ranks < 1 || sync->n_ranks > PEER_MAX_RANKS || sync->rank < 0 || sync->rank >= sync->n_ranks)
@@ -401,7 +431,7 @@ extern "C" int concord_peer_reduce_vhat(const uint16_t* own_rows, const uint16_t
     if (sync->timeout_ns <= 0) return fail(CONCORD_EINVAL, std::string(name) + ": timeout_ns must be > 0");
     if (K <= 0 || K % 8 != 0 || n_rows < 0 || n_rows > S)
         return fail(CONCORD_ESHAPE, std::string(name) + ": K must be a positive multiple of 8 and n_rows <= S");
-    if (!aligned(grad_out, 16) || (n_rows > 0 && (!aligned(own_rows, 16) || !aligned(recv, 16))))
+    if (n_rows > 0 && (!aligned(grad_out, 16) || !aligned(own_rows, 16) || !aligned(recv, 16)))
         return fail(CONCORD_EALIGN, std::string(name) + ": buffers must be 16-byte aligned");
     // a rank with no rows still takes part: one row block of masked rows gives zero partials
     int ncs, nrb; size_t off_rp, off_cp, total;

@@ -483,6 +483,60 @@ def vhat_update(grad_W, v_row, v_col, sum_v_inv, beta2=0.999, row_max=None, col_
         ws.numel(), _stream(grad_W.device)), "concord_vhat_update")
 
 
+# The layer backward's dW GEMM computes the v-hat partials in its epilogue
+# (concord_gemm_dw_vhat) instead of re-reading dW in a separate v-hat launch.
+_FUSED_DW_VHAT = True
+
+
+def set_fused_dw_vhat(enabled):
+    """Whether the layer backward uses concord_gemm_dw_vhat (dW GEMM with the
+    v-hat partials in its epilogue; default) or the dW GEMM followed by the
+    standalone v-hat launch.  The stored dW is identical either way; v-hat
+    agrees to fp32 rounding (the in-tile summation order differs)."""
+    global _FUSED_DW_VHAT
+    _FUSED_DW_VHAT = bool(enabled)
+
+
+def dw_vhat_update(grad_y_flat, x_flat, v_row, v_col, sum_v_inv, beta2=0.999, row_max=None,
+                   col_max=None, bump_salt=False):
+    """dW = dY^T X (bf16, [N, K]) and the v-hat update of vhat_update on it,
+    through concord_gemm_dw_vhat; returns dW."""
+    M, N = grad_y_flat.shape
+    K = x_flat.shape[1]
+    _need_cuda(grad_y_flat, x_flat, v_row, v_col, sum_v_inv)
+    lib = _lib()
+    dy = grad_y_flat.contiguous()
+    x = x_flat.contiguous()
+    dw = torch.empty(N, K, dtype=torch.bfloat16, device=x.device)
+    ws = _workspace("dw_vhat", lib.concord_gemm_dw_vhat_workspace_bytes(M, N, K), x.device)
+    salt = _get_step_counter(x.device) if bump_salt else None
+    _abi.check(lib.concord_gemm_dw_vhat(
+        _ptr(dy), _ptr(x), _ptr(dw), M, N, K, _ptr(v_row), _ptr(v_col), _ptr(sum_v_inv),
+        float(beta2), 1.0 - float(beta2), _ptr(row_max), _ptr(col_max), _ptr(salt), _ptr(ws),
+        ws.numel(), _stream(x.device)), "concord_gemm_dw_vhat")
+    return dw
+
+
+def _fused_dw_vhat_ok(ctx, grad_y_flat, x_flat):
+    """The backward may take the dW-with-v-hat path: the plain single-GPU
+    AdamW-family step with v-hat tracking, on bf16 CUDA operands whose
+    extents the GEMMs take (multiples of 8), on a layer large enough for the
+    epilogue form."""
+    if not _FUSED_DW_VHAT or _SIGMAG_NOISE or _sharded_of(ctx.packed_w) is not None:
+        return False
+    if not (ctx.track_adafactor_v and ctx.v_row is not None):
+        return False
+    if _COH_WEIGHTED_V and ctx.coh_pre is not None:
+        return False
+    M, N = grad_y_flat.shape
+    K = x_flat.shape[1]
+    # the epilogue form needs >= 148 output tiles of 128 x 256 (smaller layers
+    # keep the two-launch path here, as concord_gemm_dw_vhat itself would)
+    tiles = ((N + 127) // 128) * ((K + 255) // 256)
+    return (grad_y_flat.is_cuda and grad_y_flat.dtype == torch.bfloat16 and x_flat.dtype == torch.bfloat16
+            and M > 0 and M % 8 == 0 and N % 8 == 0 and K % 8 == 0 and tiles >= 148)
+
+
 def rebalance_packed(packed_w, row_exp, col_exp, row_max, col_max, MAX_M=24000, EXP_MAX=7,
                      EXP_MIN=-8, seed_buf=None, allow_tickdown=False, row_hwm=None, col_hwm=None,
                      fired_out=None, bump_seed=False, row0=0, n_total=None):
@@ -531,28 +585,31 @@ def _sharded_of(packed_w):
     return _SHARDED.get(packed_w.data_ptr()) if _SHARDED else None
 
 
-def _optimizer_half(ctx, grad_W, step_events=None):
+def _optimizer_half(ctx, grad_W, step_events=None, vhat_done=False):
     """The backward's optimizer half: this rank's row shard of the sharded
     step when the layer is data-parallel, else the single-GPU step."""
     dp = _sharded_of(ctx.packed_w)
     if dp is not None:
         dp.step(grad_W)
     else:
-        _packed_backward_step(ctx, grad_W, step_events)
+        _packed_backward_step(ctx, grad_W, step_events, vhat_done)
 
 
-def _packed_backward_step(ctx, grad_W, step_events=None):
+def _packed_backward_step(ctx, grad_W, step_events=None, vhat_done=False):
     """The optimizer half of the backward (packed_b.py:1278-1337).
 
     One launch updates v_row/v_col/sum_v_inv (and zeroes the row/col max
-    buffers, bumps the salt); one launch runs the fused packed step.
+    buffers, bumps the salt) unless `vhat_done` (the dW GEMM did it); one
+    launch runs the fused packed step.
     `step_events` (optional [_, start, end] CUDA events) bracket the step launch.
     """
     track = bool(ctx.track_rebalance)
     rmax = ctx.row_max_buf if track else None
     cmax = ctx.col_max_buf if track else None
     salt = _get_step_counter(grad_W.device)
-    if ctx.track_adafactor_v and ctx.v_row is not None:
+    if vhat_done:
+        pass
+    elif ctx.track_adafactor_v and ctx.v_row is not None:
         if _COH_WEIGHTED_V and ctx.coh_pre is not None:
             raise NotImplementedError("set_coh_weighted_v(True) is not supported by concord_b200")
         vhat_update(grad_W, ctx.v_row, ctx.v_col, ctx.sum_v_inv, ctx.adafactor_beta2,
@@ -634,10 +691,17 @@ class FusedConcordLinearPackedB(torch.autograd.Function):
         out_features, in_features = weight.shape
         x_flat = x.reshape(-1, in_features)
         grad_y_flat = grad_y.reshape(-1, out_features)
-        grad_W = _gemm.grad_weight(grad_y_flat, x_flat)
-        if _SIGMAG_NOISE:
-            grad_W = sigmag_noise(grad_W, grad_y_flat, x_flat)
-        _optimizer_half(ctx, grad_W)
+        if _fused_dw_vhat_ok(ctx, grad_y_flat, x_flat):
+            track = bool(ctx.track_rebalance)
+            grad_W = dw_vhat_update(grad_y_flat, x_flat, ctx.v_row, ctx.v_col, ctx.sum_v_inv,
+                                    ctx.adafactor_beta2, ctx.row_max_buf if track else None,
+                                    ctx.col_max_buf if track else None, bump_salt=True)
+            _packed_backward_step(ctx, grad_W, vhat_done=True)
+        else:
+            grad_W = _gemm.grad_weight(grad_y_flat, x_flat)
+            if _SIGMAG_NOISE:
+                grad_W = sigmag_noise(grad_W, grad_y_flat, x_flat)
+            _optimizer_half(ctx, grad_W)
         grad_bias = grad_y_flat.sum(0) if ctx.has_bias else None
         return (grad_x, None, None, None, grad_bias) + (None,) * 29
 
@@ -904,11 +968,15 @@ class ConcordLinearPackedB(nn.Module):
     def optimizer_step(self, grad_W, coh_stats=None, step_events=None):
         """Run the optimizer half of the backward for a given bf16 dW [N, K]
         (what the autograd backward does after its GEMMs)."""
+        _optimizer_half(self._step_ctx(coh_stats), grad_W.contiguous(), step_events)
+
+    def _step_ctx(self, coh_stats=None):
+        """The fields the backward's optimizer half reads, as the autograd ctx holds them."""
         wbuf, rmbuf, cmbuf = self._ensure_buffers()
         vals = (self.packed_w, self.row_exp, self.col_exp) + self._apply_args(wbuf, rmbuf, cmbuf)[:-1]
         ctx = SimpleNamespace(**dict(zip(_CTX_FIELDS, vals)))
         ctx.coh_stats = coh_stats if coh_stats is not None else self.coh_stats
-        _optimizer_half(ctx, grad_W.contiguous(), step_events)
+        return ctx
 
     @torch.no_grad()
     def rebalance(self, fired_out=None):

@@ -42,6 +42,8 @@
  *                            (packed_b.py:2081-2106)
  *   concord_gemm_fwd/dx/dw <- F.linear / grad_y @ W / grad_y^T @ x
  *                            (packed_b.py:1219, 1263, 1271-1277)
+ *   concord_gemm_dw_vhat  <- grad_y^T @ x followed by the v-hat update
+ *                            (packed_b.py:1271-1303) in one call
  *   concord_im2col / concord_col2im / concord_transpose_bf16
  *                         <- the data movement inside torch's
  *                            conv2d / conv2d_input used by the conv layer
@@ -462,6 +464,27 @@ int concord_gemm_dx(const uint16_t* dy, const uint16_t* w, uint16_t* dx, int64_t
                     void* workspace, size_t workspace_bytes, void* stream);
 int concord_gemm_dw(const uint16_t* dy, const uint16_t* x, uint16_t* dw, int64_t M, int64_t N, int64_t K,
                     void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * dW = dY^T X (as concord_gemm_dw) together with the v-hat update of
+ * concord_vhat_update on that dW (row/col max zeroing and salt bump
+ * included): the backward's dW GEMM (packed_b.py:1271-1277) and its
+ * Adafactor update (1278-1303) in one call.  When the N x K output has at
+ * least 148 tiles of 128 x 256 (one per SM of a B200), the squared bf16
+ * outputs are summed per tile in the GEMM's epilogue and one fold launch
+ * finishes, so dW is not read again; the dW written is bit-identical to
+ * concord_gemm_dw's, and v_row / v_col / sum_v_inv agree with
+ * concord_vhat_update's to fp32 rounding (same tiles and fold order; the
+ * in-tile order is the epilogue's).  Smaller layers run concord_gemm_dw and
+ * then concord_vhat_update (bit-identical to calling them).  `workspace`: at least
+ * concord_gemm_dw_vhat_workspace_bytes(M, N, K) bytes, 16-byte aligned,
+ * zero-filled before its first use (the call leaves it reusable).
+ */
+size_t concord_gemm_dw_vhat_workspace_bytes(int64_t M, int64_t N, int64_t K);
+int concord_gemm_dw_vhat(const uint16_t* dy, const uint16_t* x, uint16_t* dw, int64_t M, int64_t N, int64_t K,
+                         float* v_row, float* v_col, float* sum_v_inv, float beta2, float one_minus_beta2,
+                         int32_t* row_max, int32_t* col_max, int32_t* salt,
+                         void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Convolution as GEMMs (bf16, NCHW input x [B, C, H, W], kernel kh x kw,
