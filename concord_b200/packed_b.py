@@ -1195,21 +1195,3 @@ class DissipationAutoTuner:
                   f"beta1={self.committed_beta1:g} from mean coherence {window:.4f} "
                   f"over {len(self._samples)} probes in steps [{self.probe_start}, {self.probe_end})")
         return self.committed
-        if self.probe_start <= t < self.probe_end and (t - self.probe_start) % self.measure_every == 0:
-            vals = [self.meter(m) for m in self.layers]
-            if vals:
-                self._samples.append(sum(vals) / len(vals))
-        if t >= self.probe_end:
-            coh = (sum(self._samples) / len(self._samples)) if self._samples else self.table[0][0]
-            self.committed = self.kappa_from_coh(coh)
-            self.committed_beta1 = self.beta1_on \
-                if (self.beta1_on > 0 and coh >= self.beta1_coh_threshold) else 0.0
-            for m in self.layers:
-                m.gf_consol = self.committed
-                m.beta1 = self.committed_beta1
-            if self.verbose:
-                print(f"[concord] dissipation autotune: probe coh={coh:.4f} "
-                      f"-> kappa={self.committed:.0f}, beta1={self.committed_beta1:g} "
-                      f"({len(self._samples)} samples, steps {self.probe_start}-{self.probe_end})")
-            return self.committed
-        return None
