@@ -14,6 +14,11 @@ optimizer half of the layer's backward, the path this repo rebuilds:
   + v-hat 2 B/param (one read of the bf16 grad).
 The working set (~460 MB) is larger than L2 (126 MB), so no flush is needed.
 The dense GEMMs of the same layer (fwd / dX / dW) are timed beside it.
+On N > 1 GPUs that layer's update is row-sharded (strong scaling of one
+layer).  The same line carries, under `weak_scaling`, the whole-job training
+throughput of configs 5 (Llama-style decoder, tokens/s) and 4 (SDXL UNet,
+samples/s and steps/s) at this GPU count, so one run at N = 1, 2, 4, 8 gives
+their weak-scaling curves (`--no-models` skips them).
 """
 import argparse
 import json
@@ -483,20 +488,23 @@ def bench_chargpt(args, cores):
     emit(d)
 
 
-def bench_llama(args, rank, world):
-    """Config 5: weak-scaling data-parallel training step (whole job tokens/s)."""
+def bench_llama(args, rank, world, steps=None, warmup=None, ret=False):
+    """Config 5: weak-scaling data-parallel training step (whole job tokens/s).
+    With `ret` the line is returned (rank 0; None elsewhere) instead of printed."""
     import workloads
+    steps = args.steps if steps is None else steps
+    warmup = args.warmup if warmup is None else warmup
     torch.cuda.reset_peak_memory_stats()
-    r = workloads.train_llama_dp(steps=args.steps, warmup=args.warmup, batch_per_gpu=args.batch,
+    r = workloads.train_llama_dp(steps=steps, warmup=warmup, batch_per_gpu=args.batch,
                                  n_layer=args.layers, graph=args.graph)
     ms = statistics.mean(r["ms"])
     mem = torch.tensor([torch.cuda.max_memory_allocated() / 1e9], device="cuda")
     if world > 1:
         dist.all_reduce(mem, op=dist.ReduceOp.MAX)
     if rank != 0:
-        return
-    emit({"metric": "Llama-style decoder (config 5) data-parallel train tokens/s", "unit": "tokens/s",
-          "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+        return None
+    d = {"metric": "Llama-style decoder (config 5) data-parallel train tokens/s", "unit": "tokens/s",
+          "n_gpus": world, "steps": steps, "warmup": warmup, "higher_is_better": True,
           "scaling": "weak", "vs_baseline": None, "dtype": "bf16 autocast; packed int32 words",
           "data": "synthetic: uniform random token ids, vocab 32000",
           "config": {"workload": f"config 5: {args.layers}-layer d=2048 16-head SwiGLU-5504 decoder, seq 2048, "
@@ -508,23 +516,29 @@ def bench_llama(args, rank, world):
           "concord_params": r["concord_params"], "peak_mem_gb_max_rank": float(mem.item()),
           "cuda_graph": args.graph,
           "timing": "CUDA events around one training step (forward, backward with the packed steps, aux update, "
-                    "rebalance; replayed as one CUDA graph unless --no-graph), barrier before, max over ranks"})
+                    "rebalance; replayed as one CUDA graph unless --no-graph), barrier before, max over ranks"}
+    if ret:
+        return d
+    emit(d)
 
 
-def bench_sdxl(args, rank, world):
-    """Config 4: SDXL-architecture UNet training steps, weak scaling."""
+def bench_sdxl(args, rank, world, steps=None, warmup=None, ret=False):
+    """Config 4: SDXL-architecture UNet training steps, weak scaling.
+    With `ret` the line is returned (rank 0; None elsewhere) instead of printed."""
     import workloads
+    steps = args.steps if steps is None else steps
+    warmup = args.warmup if warmup is None else warmup
     batch = args.batch if args.batch != 8 else 4
-    r = workloads.train_sdxl_dp(steps=args.steps, warmup=args.warmup, batch_per_gpu=batch, gate=not args.nogate,
+    r = workloads.train_sdxl_dp(steps=steps, warmup=warmup, batch_per_gpu=batch, gate=not args.nogate,
                                 ckpt=args.ckpt, graph=args.graph)
     ms = statistics.mean(r["ms"])
     mem = torch.tensor([r["peak_gb"], r["state_gb"]], device="cuda")
     if world > 1:
         dist.all_reduce(mem, op=dist.ReduceOp.MAX)
     if rank != 0:
-        return
-    emit({"metric": "SDXL UNet train steps/s", "unit": "samples/s", "n_gpus": world, "steps": args.steps,
-          "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        return None
+    d = {"metric": "SDXL UNet train steps/s", "unit": "samples/s", "n_gpus": world, "steps": steps,
+          "warmup": warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
           "dtype": "bf16 autocast; packed int32 words", "data": "synthetic: latents, text context, pooled ~ N(0,1), "
           "t ~ U{0..999}, epsilon-prediction MSE",
           "config": {"workload": f"config 4: SDXL-architecture UNet ({r['params'] / 1e9:.3f} B params, random init), "
@@ -538,7 +552,38 @@ def bench_sdxl(args, rank, world):
           "peak_mem_gb_max_rank": float(mem[0].item()), "state_mem_gb_max_rank": float(mem[1].item()),
           "cuda_graph": args.graph,
           "timing": "CUDA events around one training step (forward, backward with the packed steps, aux update, "
-                    "rebalance; replayed as one CUDA graph unless --no-graph), barrier before, max over ranks"})
+                    "rebalance; replayed as one CUDA graph unless --no-graph), barrier before, max over ranks"}
+    if ret:
+        return d
+    emit(d)
+
+
+def model_steps(args, rank, world):
+    """The training steps of configs 5 and 4 on every rank, in the same run as
+    the packed-step line: BASELINE's scaling half ("SDXL UNet train steps/s at
+    1/2/4/8") and the data-parallel decoder, each a weak-scaling whole-job
+    figure at this GPU count.  A few timed CUDA-graph replays each (the timed
+    count is min(K, 10), after max(3, min(W, 5)) eager steps); a failure is
+    recorded in the line instead of ending the run."""
+    import gc
+    steps, warmup = max(3, min(args.steps, 10)), max(3, min(args.warmup, 5))
+    out = {"note": "whole-job weak-scaling throughput at this GPU count (fixed per-GPU batch); "
+                   "llama: config 5, 8 sequences x 2048 tokens per GPU; sdxl: config 4, 4 latents per GPU, "
+                   "coh_pre gate on; each through loss.backward() with the row-sharded packed step "
+                   f"on more than one GPU; {steps} timed steps after {warmup} eager ones"}
+    for name, fn in (("llama", bench_llama), ("sdxl", bench_sdxl)):
+        try:
+            line = fn(args, rank, world, steps=steps, warmup=warmup, ret=True)
+            if line is not None:
+                keep = ("value", "unit", "ms_per_step", "ms_per_step_all", "steps_per_s", "loss_first_last",
+                        "peak_mem_gb_max_rank", "state_mem_gb_max_rank", "concord_params")
+                out[name] = {k: line[k] for k in keep if k in line}
+                out[name]["workload"] = line["config"]["workload"]
+        except Exception as e:          # noqa: BLE001 - recorded in the line
+            out[name] = {"error": f"{type(e).__name__}: {e}"[:300]}
+        gc.collect()
+        torch.cuda.empty_cache()
+    return out
 
 
 def ms_share(part, whole):
@@ -575,6 +620,8 @@ def main():
     ap.add_argument("--rows", type=int, default=N)
     ap.add_argument("--cols", type=int, default=K)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-models", action="store_true",
+                    help="c2: skip the config 4/5 weak-scaling training steps the default line carries")
     ap.add_argument("--batch", type=int, default=8, help="llama: sequences per GPU")
     ap.add_argument("--layers", type=int, default=24, help="llama: decoder layers")
     ap.add_argument("--nogate", action="store_true", help="sdxl: disable_cohpre on every layer")
@@ -637,6 +684,7 @@ def main():
     from concord_b200 import packed_b
     packed_b._lib()
     r = bench_ours(args, rank, world, device)
+    models = None if args.no_models else model_steps(args, rank, world)
     hbm, tf, src = peaks()
     # one layer update per step whatever the GPU count (the update is sharded)
     value = r["bytes_step"] / (r["ms"] * 1e-3) / 1e9
@@ -676,6 +724,8 @@ def main():
                               "per step: [peer reduce 1] + vhat partial 1 + finish 1 + step 1 + rebalance 2; "
                               "plus NCCL collectives (not counted)"),
     })
+    if models is not None:
+        d["weak_scaling"] = models
     if world == 1:
         bms, fms = backward_time(args.rows, args.cols, device)
         packed_b.set_fused_dw_vhat(False)
