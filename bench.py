@@ -586,6 +586,61 @@ def model_steps(args, rank, world):
     return out
 
 
+CONV_SHAPES = [  # B, C, O, H=W, k (SDXL UNet channel counts, stride 1)
+    (2, 320, 320, 64, 3), (2, 640, 640, 32, 3), (2, 1280, 1280, 16, 3), (2, 320, 640, 64, 1),
+    (8, 320, 320, 64, 3), (4, 320, 320, 128, 3)]
+
+
+def bench_conv(args):
+    """The conv layer's three convolutions on one GPU, per backend: implicit
+    GEMM (channels-last, no column matrix), im2col + GEMMs, cuDNN.  CUDA
+    events, mean of 20 runs after 3 warm-ups, eager."""
+    from concord_b200 import gemm
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(20):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / 20 * 1e3
+    rows = []
+    g = torch.Generator(device="cuda").manual_seed(0)
+    for B, C, O, HW, k in CONV_SHAPES:
+        pd = k // 2
+        x = torch.randn(B, C, HW, HW, device="cuda", generator=g).to(torch.bfloat16)
+        w = (torch.randn(O, C * k * k, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+        gy = torch.randn(B, O, HW, HW, device="cuda", generator=g).to(torch.bfloat16)
+        xc, gyc = x.contiguous(memory_format=torch.channels_last), gy.contiguous(memory_format=torch.channels_last)
+        wk = gemm.filter_krsc(w, C, k, k)
+        w4 = w.view(O, C, k, k)
+        flops = 2.0 * B * HW * HW * O * C * k * k
+        r = {"shape": f"B={B} {C}->{O} {HW}x{HW} k={k}", "gflop_per_pass": flops / 1e9}
+        r["implicit_fwd_us"] = timed(lambda: gemm.conv2d_forward_nhwc(xc, wk, None, k, k, 1, pd))
+        r["implicit_bwd_us"] = timed(lambda: gemm.conv2d_backward_nhwc(xc, wk, gyc, k, k, 1, pd))
+        r["im2col_fwd_us"] = timed(lambda: gemm.conv2d_forward(x, w, None, k, k, 1, pd))
+        r["im2col_bwd_us"] = timed(lambda: gemm.conv2d_backward(x, w, gy, k, k, 1, pd))
+        r["cudnn_fwd_us"] = timed(lambda: F_conv(x, w4, pd))
+        r["cudnn_bwd_us"] = timed(lambda: (torch.nn.grad.conv2d_input(x.shape, w4, gy, padding=pd),
+                                           torch.nn.grad.conv2d_weight(x, w4.shape, gy, padding=pd)))
+        r["cudnn_cl_fwd_us"] = timed(lambda: F_conv(xc, w4.contiguous(memory_format=torch.channels_last), pd))
+        r["implicit_fwd_tflops"] = flops / (r["implicit_fwd_us"] * 1e-6) / 1e12
+        r["implicit_bwd_tflops"] = 2 * flops / (r["implicit_bwd_us"] * 1e-6) / 1e12
+        rows.append(r)
+    emit({"metric": "conv2d fwd / bwd (dX + dW) microseconds per backend", "unit": "us", "n_gpus": 1,
+          "higher_is_better": False, "data": "synthetic N(0,1) bf16", "dtype": "bf16, fp32 accumulation",
+          "config": {"workload": "ConcordConv2dPackedB's convolutions at SDXL UNet channel counts"},
+          "rows": rows})
+
+
+def F_conv(x, w4, pd):
+    return torch.nn.functional.conv2d(x, w4, padding=pd)
+
+
 def ms_share(part, whole):
     return part / whole if whole > 0 else None
 
@@ -626,11 +681,12 @@ def main():
     ap.add_argument("--layers", type=int, default=24, help="llama: decoder layers")
     ap.add_argument("--nogate", action="store_true", help="sdxl: disable_cohpre on every layer")
     ap.add_argument("--ckpt", action="store_true", help="sdxl: activation checkpointing per block")
-    ap.add_argument("--workload", default="c2", choices=["c2", "chargpt", "llama", "sdxl"],
+    ap.add_argument("--workload", default="c2", choices=["c2", "chargpt", "llama", "sdxl", "conv"],
                     help="c2: the packed-step path on config 2's largest layer (default); "
                          "chargpt: config 3's char-level GPT trained end to end; "
                          "llama: config 5's data-parallel decoder (weak scaling); "
-                         "sdxl: config 4's UNet fine-tune (weak scaling)")
+                         "sdxl: config 4's UNet fine-tune (weak scaling); "
+                         "conv: the conv layer's convolutions per backend")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="time eager launches instead of CUDA-graph replays")
     args = ap.parse_args()
@@ -671,6 +727,10 @@ def main():
     if args.workload == "chargpt":
         if rank == 0:
             bench_chargpt(args, cores)
+        return
+    if args.workload == "conv":
+        if rank == 0:
+            bench_conv(args)
         return
     if world > 1:
         torch.cuda.set_device(local)

@@ -8,7 +8,7 @@ import ctypes
 import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-ABI_VERSION = 3   # CONCORD_ABI_VERSION of include/concord_b200.h
+ABI_VERSION = 4   # CONCORD_ABI_VERSION of include/concord_b200.h
 LIB_PATH = os.path.join(_HERE, "_lib", "libconcord_b200.so")
 
 # flag bits (packed_b.py:451-458 constexprs)
@@ -28,6 +28,10 @@ KIND_SGD = 1
 ARITH_GPU = 0
 ARITH_CR = 1
 
+# implicit-GEMM convolution operators (CONCORD_CONV_*)
+CONV_FPROP = 0
+CONV_DGRAD = 1
+CONV_WGRAD = 2
 PEER_SUM_F32 = 0
 PEER_MAX_I32 = 1
 
@@ -204,6 +208,10 @@ _SIGS = [
     ("concord_col2im", ctypes.c_int,
      [_P, _I64, _I64, _I64, _I64, _I32, _I32, _I32, _I32, _I32, _I32, _P, _P]),
     ("concord_transpose_bf16", ctypes.c_int, [_P, _I64, _I64, _I64, _P, _P]),
+    ("concord_conv_nhwc_workspace_bytes", ctypes.c_size_t, [ctypes.c_int] + [_I64] * 11),
+    ("concord_conv_fprop_nhwc", ctypes.c_int, [_P, _P, _P] + [_I64] * 11 + [_P, ctypes.c_size_t, _P]),
+    ("concord_conv_dgrad_nhwc", ctypes.c_int, [_P, _P, _P] + [_I64] * 11 + [_P, ctypes.c_size_t, _P]),
+    ("concord_conv_wgrad_nhwc", ctypes.c_int, [_P, _P, _P] + [_I64] * 11 + [_P, ctypes.c_size_t, _P]),
 ]
 
 EXPORTED = [s[0] for s in _SIGS]

@@ -37,7 +37,7 @@ def _cutlass_root():
 
 
 def _flags_for(cu):
-    if os.path.basename(cu) == "gemm.cu":
+    if os.path.basename(cu) in ("gemm.cu", "convgemm.cu"):
         root = _cutlass_root()
         # tensor-core GEMMs: contraction order is the hardware's; no -fmad=false needed
         return ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",

@@ -52,9 +52,42 @@ __global__ void splitk_reduce_kernel(const float4* __restrict__ part, uint2* __r
         out[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
     }
 }
+// The TMA descriptors are encoded through the driver API, which needs a
+// current context on the calling host thread.  A thread whose first CUDA work
+// is this call (an autograd worker thread running a backward whose first node
+// is this layer, for instance) may have none bound yet; encoding then fails
+// and the kernel would run with an invalid descriptor.  When the thread has
+// no current context, bind the current device's primary context first
+// (cudaSetDevice of the device already current).  A thread with a context —
+// always the case while a stream capture is running — makes no call that
+// could implicitly synchronise.
+typedef int (*CuCtxGetCurrentFn)(void**);
+
+int bind_current_context(const char* name) {
+    static CuCtxGetCurrentFn get_current = [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            fn = nullptr;
+        return reinterpret_cast<CuCtxGetCurrentFn>(fn);
+    }();
+    if (get_current) {
+        void* ctx = nullptr;
+        if (get_current(&ctx) == 0 && ctx != nullptr) return CONCORD_OK;
+    }
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaSetDevice(dev);
+    if (e != cudaSuccess)
+        return concord::fail(CONCORD_ENODEVICE, std::string(name) + ": no usable CUDA device: " + cudaGetErrorString(e));
+    return CONCORD_OK;
+}
+
 }  // namespace concord
 
 namespace {
+using concord::bind_current_context;
 
 using namespace cute;
 
@@ -175,38 +208,6 @@ int dw_slices(int64_t M, int64_t N, int64_t K) {
     int S = 1;
     while (tiles * S * 2 <= 148 * 2 && M % (64 * S * 2) == 0 && M / (S * 2) >= 1024 && S < 16) S *= 2;
     return tiles >= 148 ? 1 : S;
-}
-
-// The TMA descriptors are encoded through the driver API, which needs a
-// current context on the calling host thread.  A thread whose first CUDA work
-// is this call (an autograd worker thread running a backward whose first node
-// is this layer, for instance) may have none bound yet; encoding then fails
-// and the kernel would run with an invalid descriptor.  When the thread has
-// no current context, bind the current device's primary context first
-// (cudaSetDevice of the device already current).  A thread with a context —
-// always the case while a stream capture is running — makes no call that
-// could implicitly synchronise.
-typedef int (*CuCtxGetCurrentFn)(void**);
-
-int bind_current_context(const char* name) {
-    static CuCtxGetCurrentFn get_current = [] {
-        void* fn = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) != cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            fn = nullptr;
-        return reinterpret_cast<CuCtxGetCurrentFn>(fn);
-    }();
-    if (get_current) {
-        void* ctx = nullptr;
-        if (get_current(&ctx) == 0 && ctx != nullptr) return CONCORD_OK;
-    }
-    int dev = -1;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e == cudaSuccess) e = cudaSetDevice(dev);
-    if (e != cudaSuccess)
-        return concord::fail(CONCORD_ENODEVICE, std::string(name) + ": no usable CUDA device: " + cudaGetErrorString(e));
-    return CONCORD_OK;
 }
 
 // D[m,n] = sum_k A[m,k] B[k,n]; strides from the problem's layouts.

@@ -205,3 +205,73 @@ def conv2d_backward(x, weight_2d, grad_y, kh, kw, stride, padding):
     _abi.check(_abi.load().concord_col2im(_ptr(dcols_t), *_geom(x, kh, kw, stride, padding), _ptr(dx),
                                           stream), "concord_col2im")
     return dx, dW
+
+
+# ---- implicit-GEMM convolutions on channels-last tensors (concord_conv_*_nhwc) ----
+
+def conv_nhwc_usable(x, weight_2d, kh, kw, stride, padding):
+    """True when the implicit-GEMM convolutions (no column matrix) can run all
+    three of this convolution's passes: channel counts multiples of 8 and
+    stride 1 (the data-gradient kernel is the stride-1 one)."""
+    if x.dim() != 4 or not _usable(x, weight_2d):
+        return False
+    B, C, H, W = x.shape
+    O, IK = weight_2d.shape
+    Ho, Wo = _conv_out(H, W, kh, kw, stride, padding)
+    return (Ho > 0 and Wo > 0 and IK == C * kh * kw and C % 8 == 0 and O % 8 == 0
+            and _pair(stride) == (1, 1))
+
+
+def _nhwc(t):
+    """[B, C, H, W] tensor as its channels-last storage viewed [B, H, W, C]
+    (a copy only when t is not already channels-last contiguous)."""
+    return t.contiguous(memory_format=torch.channels_last).permute(0, 2, 3, 1)
+
+
+def _conv_call(name, op, a, b, out, B, H, W, C, O, kh, kw, stride, padding):
+    lib = _abi.load()
+    st, pd = _pair(stride), _pair(padding)
+    dims = (B, H, W, C, O, kh, kw, st[0], st[1], pd[0], pd[1])
+    need = lib.concord_conv_nhwc_workspace_bytes(op, *dims)
+    ws = torch.empty(max(int(need), 256), dtype=torch.uint8, device=out.device)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(out.device).cuda_stream)
+    _abi.check(getattr(lib, name)(_ptr(a), _ptr(b), _ptr(out), *dims, _ptr(ws), ws.numel(), stream), name)
+
+
+def filter_krsc(weight_2d, C, kh, kw):
+    """The packed layer's [O, C*kh*kw] bf16 weight (channel, kernel row,
+    kernel column order) as the [O, kh, kw, C] filter the kernels read."""
+    O = weight_2d.shape[0]
+    return weight_2d.view(O, C, kh, kw).permute(0, 2, 3, 1).contiguous()
+
+
+def conv2d_forward_nhwc(x, w_krsc, bias, kh, kw, stride, padding):
+    """y = conv2d(x, W) without a column matrix: x read channels-last, y
+    returned as a channels-last [B, O, Ho, Wo] tensor (one bf16 rounding,
+    then the bias add)."""
+    B, C, H, W = x.shape
+    O = w_krsc.shape[0]
+    Ho, Wo = _conv_out(H, W, kh, kw, stride, padding)
+    xh = _nhwc(x)
+    y = torch.empty(B, Ho, Wo, O, dtype=torch.bfloat16, device=x.device)
+    _conv_call("concord_conv_fprop_nhwc", _abi.CONV_FPROP, xh, w_krsc, y, B, H, W, C, O, kh, kw, stride, padding)
+    y = y.permute(0, 3, 1, 2)
+    if bias is not None:
+        y.add_(bias.view(1, O, 1, 1))
+    return y
+
+
+def conv2d_backward_nhwc(x, w_krsc, grad_y, kh, kw, stride, padding):
+    """(dX, dW) without column matrices: dX channels-last [B, C, H, W] (one
+    bf16 rounding per pixel), dW the [O, C*kh*kw] bf16 matrix the packed step
+    consumes (fp32 accumulation, one rounding, permuted from the kernel's
+    [O, kh, kw, C])."""
+    B, C, H, W = x.shape
+    O = w_krsc.shape[0]
+    xh, gyh = _nhwc(x), _nhwc(grad_y)
+    dx = torch.empty(B, H, W, C, dtype=torch.bfloat16, device=x.device)
+    _conv_call("concord_conv_dgrad_nhwc", _abi.CONV_DGRAD, gyh, w_krsc, dx, B, H, W, C, O, kh, kw, stride, padding)
+    dwk = torch.empty(O, kh, kw, C, dtype=torch.bfloat16, device=x.device)
+    _conv_call("concord_conv_wgrad_nhwc", _abi.CONV_WGRAD, gyh, xh, dwk, B, H, W, C, O, kh, kw, stride, padding)
+    dW = dwk.permute(0, 3, 1, 2).reshape(O, C * kh * kw)
+    return dx.permute(0, 3, 1, 2), dW

@@ -327,19 +327,26 @@ def set_sigmag_sigma(sigma):
         t.fill_(_SIGMAG_SIGMA)
 
 
-# ConcordConv2dPackedB convolution backend: "gemm" (this package's im2col +
-# tcgen05 GEMMs, for shapes whose GEMM extents are multiples of 8) or
-# "cudnn" (torch's conv2d and its grad functions, the reference's route).
-_CONV_BACKEND = "gemm"
+# ConcordConv2dPackedB convolution backend:
+#   "implicit": implicit-GEMM convolutions on channels-last tensors (no column
+#               matrix; channel counts multiples of 8, stride 1), else "gemm"
+#   "gemm":     this package's im2col / col2im + tcgen05 GEMMs (GEMM extents
+#               multiples of 8), else cuDNN
+#   "cudnn":    torch's conv2d and its grad functions (the reference's route)
+_CONV_BACKEND = "implicit"
 
 
 def set_conv_backend(name):
-    """Choose how ConcordConv2dPackedB runs its convolutions ("gemm" or "cudnn").
-    The packed step is this package's kernels either way."""
+    """Choose how ConcordConv2dPackedB runs its convolutions ("implicit",
+    "gemm" or "cudnn").  The packed step is this package's kernels either way."""
     global _CONV_BACKEND
-    if name not in ("gemm", "cudnn"):
-        raise ValueError(f"conv backend must be 'gemm' or 'cudnn', not {name!r}")
+    if name not in ("implicit", "gemm", "cudnn"):
+        raise ValueError(f"conv backend must be 'implicit', 'gemm' or 'cudnn', not {name!r}")
     _CONV_BACKEND = name
+
+
+def get_conv_backend():
+    return _CONV_BACKEND
 
 
 def _get_sigmag_sigma(device):
@@ -1016,16 +1023,27 @@ class FusedConcordConv2dPackedB(torch.autograd.Function):
                 gf_trust_delta_sq, coh_pre, coh_stats=None):
         weight_4d = weight_buf.view(out_channels, in_channels, kh, kw)
         x_bf16 = x.to(torch.bfloat16) if x.dtype != torch.bfloat16 else x
-        x_bf16 = x_bf16.contiguous()
         bias_bf16 = (bias.to(torch.bfloat16)
                      if bias is not None and bias.dtype != torch.bfloat16 else bias)
-        ctx.gemm = _CONV_BACKEND == "gemm" and _gemm.conv_usable(x_bf16, weight_buf, kh, kw, stride, padding)
-        if ctx.gemm:
-            y = _gemm.conv2d_forward(x_bf16, weight_buf, bias_bf16, kh, kw, stride, padding)
+        ctx.implicit = _CONV_BACKEND == "implicit" and _gemm.conv_nhwc_usable(x_bf16, weight_buf, kh, kw,
+                                                                              stride, padding)
+        if ctx.implicit:
+            # channels-last activations, the filter permuted once per forward
+            x_bf16 = x_bf16.contiguous(memory_format=torch.channels_last)
+            w_krsc = _gemm.filter_krsc(weight_buf, in_channels, kh, kw)
+            ctx.gemm = False
+            y = _gemm.conv2d_forward_nhwc(x_bf16, w_krsc, bias_bf16, kh, kw, stride, padding)
+            ctx.save_for_backward(x_bf16, w_krsc)
         else:
-            y = torch.nn.functional.conv2d(x_bf16, weight_4d, bias=bias_bf16, stride=stride,
-                                           padding=padding)
-        ctx.save_for_backward(x_bf16, weight_4d)
+            x_bf16 = x_bf16.contiguous()
+            ctx.gemm = _CONV_BACKEND in ("implicit", "gemm") and _gemm.conv_usable(x_bf16, weight_buf, kh, kw,
+                                                                                   stride, padding)
+            if ctx.gemm:
+                y = _gemm.conv2d_forward(x_bf16, weight_buf, bias_bf16, kh, kw, stride, padding)
+            else:
+                y = torch.nn.functional.conv2d(x_bf16, weight_4d, bias=bias_bf16, stride=stride,
+                                               padding=padding)
+            ctx.save_for_backward(x_bf16, weight_4d)
         vals = (packed_w, row_exp, col_exp, lr, alpha, beta1, mantissa_bias, optimizer_kind,
                 weight_decay, eps, step_cap, v_scale, precond_p, gf_consol, drift_cancel_C,
                 alpha_v_fast, wd_sv, wd_sf, mass_preserve, apply_chase, track_rebalance,
@@ -1044,11 +1062,14 @@ class FusedConcordConv2dPackedB(torch.autograd.Function):
         in_c, out_c, kh, kw, stride, padding = ctx.conv
         if grad_y.dtype != torch.bfloat16:
             grad_y = grad_y.to(torch.bfloat16)
-        grad_y = grad_y.contiguous()
-        if ctx.gemm:
+        if ctx.implicit:                 # weight_4d holds the [O, kh, kw, C] filter here
+            grad_x, grad_W = _gemm.conv2d_backward_nhwc(x_bf16, weight_4d, grad_y, kh, kw, stride, padding)
+        elif ctx.gemm:
+            grad_y = grad_y.contiguous()
             grad_x, grad_W = _gemm.conv2d_backward(x_bf16, weight_4d.view(out_c, -1), grad_y, kh, kw,
                                                    stride, padding)
         else:
+            grad_y = grad_y.contiguous()
             grad_x = torch.nn.grad.conv2d_input(x_bf16.shape, weight_4d, grad_y, stride=stride,
                                                 padding=padding)
             grad_W = torch.nn.grad.conv2d_weight(x_bf16, (out_c, in_c, kh, kw), grad_y,

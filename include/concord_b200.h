@@ -62,7 +62,7 @@
 extern "C" {
 #endif
 
-#define CONCORD_ABI_VERSION 3
+#define CONCORD_ABI_VERSION 4
 
 /* status codes */
 #define CONCORD_OK            0
@@ -506,6 +506,36 @@ int concord_col2im(const uint16_t* dcols_t, int64_t B, int64_t C, int64_t H, int
  * <= 65535. */
 int concord_transpose_bf16(const uint16_t* in, int64_t batches, int64_t R, int64_t C, uint16_t* out,
                            void* stream);
+
+/*
+ * Implicit-GEMM convolutions on channels-last (NHWC) bf16 tensors
+ * (fp32 accumulation, one round-to-nearest-even per output element), with
+ * no column matrix: the activation is read by TMA in im2col mode.  They
+ * replace the reference conv layer's cuDNN calls, F.conv2d
+ * (concord/packed_b.py:1890) and torch.nn.grad.conv2d_input /
+ * conv2d_weight (packed_b.py:1939-1947).
+ *   x  [B, H, W, C]      dx the same;  y / dy [B, Ho, Wo, O]
+ *   w  [O, kh, kw, C]    (KRSC: the packed [O, C*kh*kw] weight permuted)
+ *   dw [O, kh, kw, C]    (wgrad writes KRSC; the packed step reads KCRS)
+ * C % 8 == 0, O % 8 == 0, every tensor 16-byte aligned; dgrad needs stride
+ * 1.  Workspace: concord_conv_nhwc_workspace_bytes(op, ...) bytes (wgrad
+ * splits its B*Ho*Wo reduction when the output has few tiles; its
+ * split-ordered fixup is deterministic).
+ */
+#define CONCORD_CONV_FPROP 0
+#define CONCORD_CONV_DGRAD 1
+#define CONCORD_CONV_WGRAD 2
+size_t concord_conv_nhwc_workspace_bytes(int op, int64_t B, int64_t H, int64_t W, int64_t C, int64_t O,
+                                         int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw);
+int concord_conv_fprop_nhwc(const uint16_t* x, const uint16_t* w, uint16_t* y, int64_t B, int64_t H, int64_t W,
+                            int64_t C, int64_t O, int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph,
+                            int64_t pw, void* workspace, size_t workspace_bytes, void* stream);
+int concord_conv_dgrad_nhwc(const uint16_t* dy, const uint16_t* w, uint16_t* dx, int64_t B, int64_t H, int64_t W,
+                            int64_t C, int64_t O, int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph,
+                            int64_t pw, void* workspace, size_t workspace_bytes, void* stream);
+int concord_conv_wgrad_nhwc(const uint16_t* dy, const uint16_t* x, uint16_t* dw, int64_t B, int64_t H, int64_t W,
+                            int64_t C, int64_t O, int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph,
+                            int64_t pw, void* workspace, size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -79,7 +79,16 @@ def test_conv_gemm_matches_fp32_conv(case):
     assert (dx.float() - dx_ref).abs().max().item() <= 2.0 ** -6 * dx_ref.abs().max().item()
 
 
-def test_conv_layer_step_equals_linear_on_unfolded_input():
+@pytest.fixture
+def im2col_backend():
+    import concord_b200
+    old = concord_b200.get_conv_backend()
+    concord_b200.set_conv_backend("gemm")
+    yield
+    concord_b200.set_conv_backend(old)
+
+
+def test_conv_layer_step_equals_linear_on_unfolded_input(im2col_backend):
     from concord_b200 import ConcordConv2dPackedB, ConcordLinearPackedB, gemm
     from concord_b200.checkpoint import set_step_salt
     B, C, H, W, O, k = 2, 16, 12, 12, 32, 3
@@ -129,6 +138,7 @@ def test_cudnn_backend_switch():
         dws.append(grad_W.float().clone())
         return orig_step(ctx, grad_W, *rest)
     gemm.conv2d_backward, pb._packed_backward_step = spy_bwd, spy_step
+    default = concord_b200.get_conv_backend()
     try:
         for backend in ("cudnn", "gemm"):
             concord_b200.set_conv_backend(backend)
@@ -142,7 +152,7 @@ def test_cudnn_backend_switch():
         assert (dws[0] - dws[1]).abs().max().item() <= 2.0 ** -7 * dws[1].abs().max().item()
     finally:
         gemm.conv2d_backward, pb._packed_backward_step = orig_bwd, orig_step
-        concord_b200.set_conv_backend("gemm")
+        concord_b200.set_conv_backend(default)
     with pytest.raises(ValueError):
         concord_b200.set_conv_backend("winograd")
 

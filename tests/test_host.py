@@ -32,7 +32,7 @@ def test_library_exports_header_symbols(built):
     assert declared == exported
     assert declared == set(_abi.EXPORTED)
     _abi.load()
-    assert _abi.load().concord_abi_version() == _abi.ABI_VERSION == 3
+    assert _abi.load().concord_abi_version() == _abi.ABI_VERSION == 4
 
 
 def test_gemm_dw_split_decision(built):
