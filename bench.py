@@ -530,7 +530,7 @@ def bench_sdxl(args, rank, world, steps=None, warmup=None, ret=False):
     warmup = args.warmup if warmup is None else warmup
     batch = args.batch if args.batch != 8 else 4
     r = workloads.train_sdxl_dp(steps=steps, warmup=warmup, batch_per_gpu=batch, gate=not args.nogate,
-                                ckpt=args.ckpt, graph=args.graph)
+                                ckpt=args.ckpt, graph=args.graph, channels_last=not args.nchw)
     ms = statistics.mean(r["ms"])
     mem = torch.tensor([r["peak_gb"], r["state_gb"]], device="cuda")
     if world > 1:
@@ -545,7 +545,9 @@ def bench_sdxl(args, rank, world, steps=None, warmup=None, ret=False):
                                  f"latents [{batch},4,128,128] per GPU, Concord on all {r['n_layers']} Linear and conv "
                                  f"layers ({r['concord_params'] / 1e9:.3f} B params), coh_pre gate "
                                  f"{'off' if args.nogate else 'on'}, activation checkpointing "
-                                 f"{'on' if args.ckpt else 'off'}, lr 5e-5",
+                                 f"{'on' if args.ckpt else 'off'}, lr 5e-5, "
+                                 f"{'NCHW' if args.nchw else 'channels-last'} activations, conv backend "
+                                 f"{__import__('concord_b200').get_conv_backend()}",
                      "global_batch": batch * world, "parallelism": f"dp{world}"},
           "value": r["samples_per_step"] / (ms * 1e-3), "steps_per_s": 1e3 / ms, "ms_per_step": ms,
           "ms_per_step_all": r["ms"], "loss_first_last": [r["losses"][0], r["losses"][-1]],
@@ -610,7 +612,9 @@ def bench_conv(args):
         return e0.elapsed_time(e1) / 20 * 1e3
     rows = []
     g = torch.Generator(device="cuda").manual_seed(0)
-    for B, C, O, HW, k in CONV_SHAPES:
+    shapes = CONV_SHAPES if not args.conv_shapes else \
+        [tuple(int(v) for v in sh.split(",")) for sh in args.conv_shapes.split(";")]
+    for B, C, O, HW, k in shapes:
         pd = k // 2
         x = torch.randn(B, C, HW, HW, device="cuda", generator=g).to(torch.bfloat16)
         w = (torch.randn(O, C * k * k, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
@@ -687,9 +691,17 @@ def main():
                          "llama: config 5's data-parallel decoder (weak scaling); "
                          "sdxl: config 4's UNet fine-tune (weak scaling); "
                          "conv: the conv layer's convolutions per backend")
+    ap.add_argument("--conv-backend", default=None, choices=["implicit", "gemm", "cudnn"],
+                    help="sdxl/conv: ConcordConv2dPackedB's convolution backend (default: the package's)")
+    ap.add_argument("--nchw", action="store_true", help="sdxl: NCHW activations instead of channels-last")
+    ap.add_argument("--conv-shapes", default=None,
+                    help="conv: ';'-separated B,C,O,HW,k shapes instead of the default list")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="time eager launches instead of CUDA-graph replays")
     args = ap.parse_args()
+    if args.conv_backend:
+        import concord_b200
+        concord_b200.set_conv_backend(args.conv_backend)
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

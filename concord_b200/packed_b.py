@@ -1035,9 +1035,14 @@ class FusedConcordConv2dPackedB(torch.autograd.Function):
             y = _gemm.conv2d_forward_nhwc(x_bf16, w_krsc, bias_bf16, kh, kw, stride, padding)
             ctx.save_for_backward(x_bf16, w_krsc)
         else:
-            x_bf16 = x_bf16.contiguous()
-            ctx.gemm = _CONV_BACKEND in ("implicit", "gemm") and _gemm.conv_usable(x_bf16, weight_buf, kh, kw,
-                                                                                   stride, padding)
+            # a channels-last input on the implicit backend whose convolution the
+            # implicit GEMM does not run (odd channel counts, strides) goes to cuDNN
+            # in channels-last rather than through an NCHW column matrix
+            cl = (_CONV_BACKEND == "implicit" and not x_bf16.is_contiguous()
+                  and x_bf16.is_contiguous(memory_format=torch.channels_last))
+            x_bf16 = x_bf16.contiguous(memory_format=torch.channels_last) if cl else x_bf16.contiguous()
+            ctx.gemm = (not cl and _CONV_BACKEND in ("implicit", "gemm")
+                        and _gemm.conv_usable(x_bf16, weight_buf, kh, kw, stride, padding))
             if ctx.gemm:
                 y = _gemm.conv2d_forward(x_bf16, weight_buf, bias_bf16, kh, kw, stride, padding)
             else:

@@ -548,7 +548,7 @@ def sdxl_batch(B, gen, device, res=128):
 
 
 def train_sdxl_dp(steps, warmup, batch_per_gpu=4, res=128, lr=5e-5, aux_lr=1e-4, seed=0, group=None,
-                  gate=True, ckpt=False, graph=True):
+                  gate=True, ckpt=False, graph=True, channels_last=True):
     """Config 4: epsilon-prediction MSE fine-tune steps of the SDXL-architecture
     UNet (~2.6 B parameters, random init), bf16 autocast, Concord on every
     Linear and every convolution (3x3 ones as their reshaped [O, I*9] weight),
@@ -557,7 +557,9 @@ def train_sdxl_dp(steps, warmup, batch_per_gpu=4, res=128, lr=5e-5, aux_lr=1e-4,
     loss.backward()) and the other parameters' gradients are all-reduced.
     Weak scaling: `batch_per_gpu` samples per GPU.  lr 5e-5 is the
     reference's SDXL setting (notebook/src/sdxl_train.py:154); `ckpt` recomputes
-    every block in the backward (activation checkpointing)."""
+    every block in the backward (activation checkpointing).  `channels_last`
+    keeps the activations NHWC end to end (the latents and every conv output),
+    the layout the implicit-GEMM convolutions read and write without copies."""
     import torch.distributed as dist
     from concord_b200.convert import concordify
     world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -565,6 +567,8 @@ def train_sdxl_dp(steps, warmup, batch_per_gpu=4, res=128, lr=5e-5, aux_lr=1e-4,
     dev = torch.device("cuda", torch.cuda.current_device())
     torch.manual_seed(seed)
     model = SDXLUNet().to(dev)
+    if channels_last:
+        model = model.to(memory_format=torch.channels_last)
     model.ckpt = ckpt
     n_total = sum(p.numel() for p in model.parameters())
     layers = concordify(model, lr=lr, convs=True)
@@ -583,6 +587,9 @@ def train_sdxl_dp(steps, warmup, batch_per_gpu=4, res=128, lr=5e-5, aux_lr=1e-4,
     base_mem = torch.cuda.memory_allocated()
     torch.cuda.reset_peak_memory_stats()
     static = [t.clone() for t in sdxl_batch(batch_per_gpu, g, dev, res)]
+    if channels_last:                         # latents and noise NHWC
+        static[0] = static[0].contiguous(memory_format=torch.channels_last)
+        static[4] = static[4].contiguous(memory_format=torch.channels_last)
 
     def refill(it):
         lat, ctx, pooled, t, noise, ids = sdxl_batch(batch_per_gpu, g, dev, res)
