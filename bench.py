@@ -641,6 +641,57 @@ def bench_conv(args):
           "rows": rows})
 
 
+def bench_gemm(args):
+    """The layer's three GEMMs at config 2's largest shape (M=8192 tokens,
+    K=2048, N=10240) per implementation: this package's 2-SM tcgen05 kernel
+    (concord_gemm2sm), the CUTLASS 1-SM kernels, cuBLAS (torch).  CUDA events,
+    mean of 20 after 3 warm-ups, eager."""
+    import ctypes
+    from concord_b200 import _abi, gemm
+    lib = _abi.load()
+    Mt, Kt, Nt = M, args.cols, args.rows
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(Mt, Kt, device="cuda", generator=g).to(torch.bfloat16)
+    w = (torch.randn(Nt, Kt, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    dy = torch.randn(Mt, Nt, device="cuda", generator=g).to(torch.bfloat16)
+    y = torch.empty(Mt, Nt, dtype=torch.bfloat16, device="cuda")
+    dx = torch.empty(Mt, Kt, dtype=torch.bfloat16, device="cuda")
+    dw = torch.empty(Nt, Kt, dtype=torch.bfloat16, device="cuda")
+    s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def p(t):
+        return ctypes.c_void_p(t.data_ptr())
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(20):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / 20
+    runs = {
+        "2sm_fwd": lambda: lib.concord_gemm2sm(p(x), 0, Kt, p(w), 0, Kt, p(y), Nt, Mt, Nt, Kt, s),
+        "2sm_dx": lambda: lib.concord_gemm2sm(p(dy), 0, Nt, p(w), 1, Kt, p(dx), Kt, Mt, Kt, Nt, s),
+        "2sm_dw": lambda: lib.concord_gemm2sm(p(dy), 1, Nt, p(x), 1, Kt, p(dw), Kt, Nt, Kt, Mt, s),
+        "cutlass1sm_fwd": lambda: gemm.forward(x, w), "cutlass1sm_dx": lambda: gemm.grad_input(dy, w),
+        "cutlass1sm_dw": lambda: gemm.grad_weight(dy, x),
+        "cublas_fwd": lambda: x @ w.T, "cublas_dx": lambda: dy @ w, "cublas_dw": lambda: dy.T @ x}
+    flops = 2.0 * Mt * Nt * Kt
+    out = {}
+    for k, fn in runs.items():
+        ms = timed(fn)
+        out[k] = {"us": ms * 1e3, "tflops": flops / (ms * 1e-3) / 1e12}
+    torch.cuda.synchronize()
+    emit({"metric": "layer GEMM TFLOP/s per implementation", "unit": "TFLOP/s", "n_gpus": 1,
+          "higher_is_better": True, "data": "synthetic N(0,1) bf16", "dtype": "bf16, fp32 accumulation",
+          "config": {"workload": f"config 2 largest layer: M={Mt}, K={Kt}, N={Nt}"}, "results": out,
+          "gemm2sm_error_word": int(lib.concord_gemm2sm_error(1)), "gemm2sm_pairs": int(lib.concord_gemm2sm_pairs())})
+
+
 def F_conv(x, w4, pd):
     return torch.nn.functional.conv2d(x, w4, padding=pd)
 
@@ -685,12 +736,13 @@ def main():
     ap.add_argument("--layers", type=int, default=24, help="llama: decoder layers")
     ap.add_argument("--nogate", action="store_true", help="sdxl: disable_cohpre on every layer")
     ap.add_argument("--ckpt", action="store_true", help="sdxl: activation checkpointing per block")
-    ap.add_argument("--workload", default="c2", choices=["c2", "chargpt", "llama", "sdxl", "conv"],
+    ap.add_argument("--workload", default="c2", choices=["c2", "chargpt", "llama", "sdxl", "conv", "gemm"],
                     help="c2: the packed-step path on config 2's largest layer (default); "
                          "chargpt: config 3's char-level GPT trained end to end; "
                          "llama: config 5's data-parallel decoder (weak scaling); "
                          "sdxl: config 4's UNet fine-tune (weak scaling); "
-                         "conv: the conv layer's convolutions per backend")
+                         "conv: the conv layer's convolutions per backend; "
+                         "gemm: the layer's GEMMs per implementation")
     ap.add_argument("--conv-backend", default=None, choices=["implicit", "gemm", "cudnn"],
                     help="sdxl/conv: ConcordConv2dPackedB's convolution backend (default: the package's)")
     ap.add_argument("--nchw", action="store_true", help="sdxl: NCHW activations instead of channels-last")
@@ -743,6 +795,10 @@ def main():
     if args.workload == "conv":
         if rank == 0:
             bench_conv(args)
+        return
+    if args.workload == "gemm":
+        if rank == 0:
+            bench_gemm(args)
         return
     if world > 1:
         torch.cuda.set_device(local)

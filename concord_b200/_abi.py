@@ -28,6 +28,9 @@ KIND_SGD = 1
 ARITH_GPU = 0
 ARITH_CR = 1
 
+# kernels behind concord_gemm_fwd/dx/dw (CONCORD_GEMM_*)
+GEMM_2SM = 0
+GEMM_CUTLASS = 1
 # implicit-GEMM convolution operators (CONCORD_CONV_*)
 CONV_FPROP = 0
 CONV_DGRAD = 1
@@ -208,6 +211,11 @@ _SIGS = [
     ("concord_col2im", ctypes.c_int,
      [_P, _I64, _I64, _I64, _I64, _I32, _I32, _I32, _I32, _I32, _I32, _P, _P]),
     ("concord_transpose_bf16", ctypes.c_int, [_P, _I64, _I64, _I64, _P, _P]),
+    ("concord_gemm2sm", ctypes.c_int, [_P, _I32, _I64, _P, _I32, _I64, _P, _I64, _I64, _I64, _I64, _P]),
+    ("concord_gemm2sm_error", ctypes.c_int, [_I32]),
+    ("concord_gemm2sm_pairs", ctypes.c_int, []),
+    ("concord_gemm_set_impl", ctypes.c_int, [_I32]),
+    ("concord_gemm_get_impl", ctypes.c_int, []),
     ("concord_conv_nhwc_workspace_bytes", ctypes.c_size_t, [ctypes.c_int] + [_I64] * 11),
     ("concord_conv_fprop_nhwc", ctypes.c_int, [_P, _P, _P] + [_I64] * 11 + [_P, ctypes.c_size_t, _P]),
     ("concord_conv_dgrad_nhwc", ctypes.c_int, [_P, _P, _P] + [_I64] * 11 + [_P, ctypes.c_size_t, _P]),

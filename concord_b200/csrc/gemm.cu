@@ -23,6 +23,8 @@
 #include <stdlib.h>
 
 #include <algorithm>
+#include <atomic>
+#include <string>
 
 #include "cute/tensor.hpp"
 #include "cutlass/cutlass.h"
@@ -313,13 +315,48 @@ int run_gemm_dw_vhat(const void* dy, const void* x, void* dw, int N, int K, int 
 
 bool bad(const void* p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) % 16) != 0; }
 
+// which kernels the plain GEMM entry points run: CONCORD_GEMM_2SM (the
+// package's own 2-SM kernel, gemm2sm.cu; default) or CONCORD_GEMM_CUTLASS
+// (the CUTLASS 1-SM kernels above).  CONCORD_GEMM_IMPL=cutlass in the
+// environment changes the default.
+std::atomic<int> g_impl{-1};
+int gemm_impl() {
+    int v = g_impl.load();
+    if (v < 0) {
+        const char* e = getenv("CONCORD_GEMM_IMPL");
+        v = (e && std::string(e) == "cutlass") ? CONCORD_GEMM_CUTLASS : CONCORD_GEMM_2SM;
+        int expect = -1;
+        g_impl.compare_exchange_strong(expect, v);
+        v = g_impl.load();
+    }
+    return v;
+}
+
 }  // namespace
+
+namespace concord {
+int gemm2sm(const void* A, int a_mn, int64_t lda, const void* B, int b_mn, int64_t ldb, void* D, int64_t ldd,
+            int64_t M, int64_t N, int64_t K, cudaStream_t stream, const char* name, float* rp = nullptr,
+            int64_t ldrp = 0, float* cp = nullptr, int64_t ldcp = 0);
+}
+
+extern "C" int concord_gemm_set_impl(int32_t impl) {
+    if (impl != CONCORD_GEMM_2SM && impl != CONCORD_GEMM_CUTLASS)
+        return concord::fail(CONCORD_EINVAL, "concord_gemm_set_impl: impl must be CONCORD_GEMM_2SM or CONCORD_GEMM_CUTLASS");
+    g_impl.store(impl);
+    return CONCORD_OK;
+}
+
+extern "C" int concord_gemm_get_impl(void) { return gemm_impl(); }
 
 // Y[M,N] = X[M,K] W[N,K]^T
 extern "C" int concord_gemm_fwd(const uint16_t* x, const uint16_t* w, uint16_t* y, int64_t M, int64_t N, int64_t K,
                                 void* workspace, size_t workspace_bytes, void* stream) {
     if (bad(x) || bad(w) || bad(y)) return concord::fail(CONCORD_EALIGN, "concord_gemm_fwd: null or unaligned pointer");
     if (M <= 0 || N <= 0 || K <= 0) return concord::fail(CONCORD_ESHAPE, "concord_gemm_fwd: bad shape");
+    if (gemm_impl() == CONCORD_GEMM_2SM)      // x K-major [M,K], w K-major [N,K]
+        return concord::gemm2sm(x, 0, K, w, 0, K, y, N, M, N, K, reinterpret_cast<cudaStream_t>(stream),
+                                "concord_gemm_fwd");
     return run_gemm<GemmFwd>(x, w, y, (int)M, (int)N, (int)K, workspace, workspace_bytes,
                              reinterpret_cast<cudaStream_t>(stream), false, nullptr, "concord_gemm_fwd");
 }
@@ -329,6 +366,9 @@ extern "C" int concord_gemm_dx(const uint16_t* dy, const uint16_t* w, uint16_t* 
                                void* workspace, size_t workspace_bytes, void* stream) {
     if (bad(dy) || bad(w) || bad(dx)) return concord::fail(CONCORD_EALIGN, "concord_gemm_dx: null or unaligned pointer");
     if (M <= 0 || N <= 0 || K <= 0) return concord::fail(CONCORD_ESHAPE, "concord_gemm_dx: bad shape");
+    if (gemm_impl() == CONCORD_GEMM_2SM)      // dy K-major [M,N], w MN-major ([N,K]: k=N rows, n=K contiguous)
+        return concord::gemm2sm(dy, 0, N, w, 1, K, dx, K, M, K, N, reinterpret_cast<cudaStream_t>(stream),
+                                "concord_gemm_dx");
     return run_gemm<GemmDx>(dy, w, dx, (int)M, (int)K, (int)N, workspace, workspace_bytes,
                             reinterpret_cast<cudaStream_t>(stream), false, nullptr, "concord_gemm_dx");
 }
@@ -339,6 +379,9 @@ extern "C" int concord_gemm_dw(const uint16_t* dy, const uint16_t* x, uint16_t* 
     if (bad(dy) || bad(x) || bad(dw)) return concord::fail(CONCORD_EALIGN, "concord_gemm_dw: null or unaligned pointer");
     if (M <= 0 || N <= 0 || K <= 0) return concord::fail(CONCORD_ESHAPE, "concord_gemm_dw: bad shape");
     const int S = dw_slices(M, N, K);
+    if (S == 1 && gemm_impl() == CONCORD_GEMM_2SM)   // dy MN-major ([M,N]: k=M rows), x MN-major ([M,K])
+        return concord::gemm2sm(dy, 1, N, x, 1, K, dw, K, N, K, M, reinterpret_cast<cudaStream_t>(stream),
+                                "concord_gemm_dw");
     if (S == 1)
         return run_gemm<GemmDw>(dy, x, dw, (int)N, (int)K, (int)M, workspace, workspace_bytes,
                                 reinterpret_cast<cudaStream_t>(stream), false, nullptr, "concord_gemm_dw");
@@ -439,7 +482,10 @@ extern "C" int concord_gemm_dw_vhat(const uint16_t* dy, const uint16_t* x, uint1
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     float* rp = reinterpret_cast<float*>(ws + L.off_rp);
     float* cp = reinterpret_cast<float*>(ws + L.off_cp);
-    if (int rc = run_gemm_dw_vhat(dy, x, dw, (int)N, (int)K, (int)M, rp, cp, ws + L.off_gemm,
+    if (gemm_impl() == CONCORD_GEMM_2SM) {
+        // the package's 2-SM dW (dy MN-major, x MN-major) with the partials in its epilogue
+        if (int rc = concord::gemm2sm(dy, 1, N, x, 1, K, dw, K, N, K, M, st, name, rp, L.ldrp, cp, L.ldcp)) return rc;
+    } else if (int rc = run_gemm_dw_vhat(dy, x, dw, (int)N, (int)K, (int)M, rp, cp, ws + L.off_gemm,
                                   workspace_bytes - L.off_gemm, st, false, nullptr))
         return rc;
     return concord::vhat_fold_partials(rp, L.ldrp, cp, L.ldcp, N, K, v_row, v_col, sum_v_inv, beta2,

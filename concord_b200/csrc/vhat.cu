@@ -57,16 +57,20 @@ struct VhatArgs {
 // rows of a warp whose loads go out together: 8 for a local gradient, fewer
 // when each row is the sum of P ranks' rows
 template <int P>
-struct VhGroup { static constexpr int G = P == 0 ? 8 : (P <= 4 ? 2 : 1); };
+struct VhGroup { static constexpr int G = P == 0 ? 4 : (P <= 4 ? 2 : 1); };
 
-constexpr int VH_BLOCKS_PER_SM = 3;
+// resident blocks per SM: the local form (P == 0) keeps a whole C2-sized
+// layer's tiles (640) resident in one wave (5 x 148 blocks); the peer forms
+// hold more sources in flight per thread
+template <int P>
+struct VhOcc { static constexpr int B = P == 0 ? 5 : 3; };
 
 // Persistent: block b takes tiles b, b + gridDim.x, ...; tile t covers
 // column slab t % ncs and row block t / ncs.  Which block computes a tile
 // changes nothing in the arithmetic: every partial and every final sum has
 // a fixed order.
 template <int P>
-__global__ void __launch_bounds__(VH_THREADS, VH_BLOCKS_PER_SM) vhat_kernel(VhatArgs A) {
+__global__ void __launch_bounds__(VH_THREADS, VhOcc<P>::B) vhat_kernel(VhatArgs A) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     __shared__ float colsm[VH_THREADS / 32][VH_COLS];
 
@@ -351,15 +355,15 @@ static void vhat_layout(int64_t N, int64_t K, int* ncs, int* nrb, size_t* off_rp
     *total = *off_cp + (size_t)(*nrb) * (size_t)K * sizeof(float);
 }
 
-// one block per tile up to VH_BLOCKS_PER_SM resident blocks on every SM
-static unsigned vhat_grid(int ncs, int nrb) {
+// one block per tile up to `per_sm` resident blocks on every SM
+static unsigned vhat_grid(int ncs, int nrb, int per_sm) {
     static const int sms = [] {
         int dev = 0, n = 148;
         if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
         return n > 0 ? n : 148;
     }();
     const int64_t tiles = (int64_t)ncs * nrb;
-    const int64_t cap = (int64_t)sms * VH_BLOCKS_PER_SM;
+    const int64_t cap = (int64_t)sms * per_sm;
     return (unsigned)(tiles < cap ? tiles : cap);
 }
 
@@ -386,7 +390,7 @@ static int vhat_launch(const uint16_t* grad, int64_t ldg, int64_t N, int64_t K, 
                reinterpret_cast<unsigned*>(ws), ncs, nrb,
                (K % 8 == 0) && (ldg % 8 == 0) && aligned(grad, 16), col_sum_out, vsum_out,
                nullptr, nullptr, 0, PeerSync{}};
-    vhat_kernel<0><<<vhat_grid(ncs, nrb), VH_THREADS, 0, as_stream(stream)>>>(A);
+    vhat_kernel<0><<<vhat_grid(ncs, nrb, VhOcc<0>::B), VH_THREADS, 0, as_stream(stream)>>>(A);
     vhat_fold(A, nullptr, as_stream(stream));
     return check_launch(name);
 }
@@ -445,7 +449,7 @@ extern "C" int concord_peer_reduce_vhat(const uint16_t* own_rows, const uint16_t
                reinterpret_cast<float*>(ws + off_rp), reinterpret_cast<float*>(ws + off_cp),
                reinterpret_cast<unsigned*>(ws), ncs, nrb, true, col_sum_out, vsum_out, own_rows, recv, S,
                PeerSync{sync->flags, sync->peer_flags, sync->state, sync->rank, sync->n_ranks, sync->timeout_ns}};
-    const unsigned grid = vhat_grid(ncs, nrb);
+    const unsigned grid = vhat_grid(ncs, nrb, VhOcc<1>::B);
     cudaStream_t st = as_stream(stream);
     switch (sync->n_ranks) {
         case 1: launch_peer_vhat<1>(grid, st, A); break;

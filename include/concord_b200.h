@@ -508,6 +508,31 @@ int concord_transpose_bf16(const uint16_t* in, int64_t batches, int64_t R, int64
                            void* stream);
 
 /*
+ * 2-SM tcgen05 GEMM written in this package (no CUTLASS): D[M,N] (bf16,
+ * row-major, row stride ldd) = sum_k A(m,k) B(n,k), fp32 accumulation, one
+ * RNE rounding.  a_mn = 0: A is K-major, the row-major [M, K] matrix (row
+ * stride lda); a_mn = 1: A is MN-major, the row-major [K, M] matrix.  B
+ * likewise with N.  Extents and strides multiples of 8, 16-byte aligned.
+ * The layer's three GEMMs (packed_b.py:1219, 1263, 1273) are
+ *   fwd (x K-major, w K-major), dX (dY K-major, w MN-major),
+ *   dW (dY MN-major, x MN-major).
+ * concord_gemm2sm_error(reset): the device's error word (non-zero when a
+ * barrier wait inside the kernel ran out; 2 s of GPU time per wait).
+ */
+/* Kernels behind concord_gemm_fwd / _dx / _dw (process-wide; the split-K dW
+ * and concord_gemm_dw_vhat always run the CUTLASS kernels):
+ * CONCORD_GEMM_2SM (default) or CONCORD_GEMM_CUTLASS. */
+#define CONCORD_GEMM_2SM 0
+#define CONCORD_GEMM_CUTLASS 1
+int concord_gemm_set_impl(int32_t impl);
+int concord_gemm_get_impl(void);
+int concord_gemm2sm(const uint16_t* a, int32_t a_mn, int64_t lda, const uint16_t* b, int32_t b_mn, int64_t ldb,
+                    uint16_t* d, int64_t ldd, int64_t M, int64_t N, int64_t K, void* stream);
+int concord_gemm2sm_error(int32_t reset);
+/* CTA pairs the 2-SM GEMM keeps resident (its persistent grid). */
+int concord_gemm2sm_pairs(void);
+
+/*
  * Implicit-GEMM convolutions on channels-last (NHWC) bf16 tensors
  * (fp32 accumulation, one round-to-nearest-even per output element), with
  * no column matrix: the activation is read by TMA in im2col mode.  They

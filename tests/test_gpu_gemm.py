@@ -24,8 +24,21 @@ def _close(got, ref, absprod, K):
     assert bool((err <= tol).all()), float((err / tol).max())
 
 
+@pytest.fixture(params=["2sm", "cutlass"])
+def impl(request):
+    """Both kernel families behind concord_gemm_fwd/dx/dw: the package's own
+    2-SM kernel (default) and the CUTLASS 1-SM kernels."""
+    from concord_b200 import _abi
+    lib = _abi.load()
+    old = lib.concord_gemm_get_impl()
+    _abi.check(lib.concord_gemm_set_impl(_abi.GEMM_2SM if request.param == "2sm" else _abi.GEMM_CUTLASS),
+               "concord_gemm_set_impl")
+    yield request.param
+    lib.concord_gemm_set_impl(old)
+
+
 @pytest.mark.parametrize("M,N,K", SHAPES)
-def test_gemm_fwd_dx_dw(M, N, K):
+def test_gemm_fwd_dx_dw(M, N, K, impl):
     from concord_b200 import gemm
     g = torch.Generator(device=DEV).manual_seed(M + N + K)
     x = torch.randn(M, K, generator=g, device=DEV).to(torch.bfloat16)
