@@ -682,9 +682,12 @@ def bench_gemm(args):
         "cublas_fwd": lambda: x @ w.T, "cublas_dx": lambda: dy @ w, "cublas_dw": lambda: dy.T @ x}
     flops = 2.0 * Mt * Nt * Kt
     out = {}
+    old_impl = lib.concord_gemm_get_impl()
     for k, fn in runs.items():
+        lib.concord_gemm_set_impl(_abi.GEMM_CUTLASS if k.startswith("cutlass") else _abi.GEMM_2SM)
         ms = timed(fn)
         out[k] = {"us": ms * 1e3, "tflops": flops / (ms * 1e-3) / 1e12}
+    lib.concord_gemm_set_impl(old_impl)
     torch.cuda.synchronize()
     emit({"metric": "layer GEMM TFLOP/s per implementation", "unit": "TFLOP/s", "n_gpus": 1,
           "higher_is_better": True, "data": "synthetic N(0,1) bf16", "dtype": "bf16, fp32 accumulation",

@@ -19,8 +19,9 @@
 // (multicast to both CTAs' barriers) frees a ring slot once the MMAs reading
 // it are done.  Tensor memory holds two 256-column accumulators, so the four
 // epilogue warps of each CTA drain one tile (`tcgen05.ld`, bf16 rounding,
-// 16-byte stores) while the next tile accumulates.  Persistent: pair p takes
-// tiles p, p + pairs, ...
+// each warp's 32 x 32 pieces staged in shared memory and written by TMA tile
+// stores) while the next tile accumulates.  Persistent: pair p takes tiles
+// p, p + pairs, ...
 //
 // Every wait on a barrier is bounded: after 2 s of GPU time it records an
 // error word and that role stops; the others then run out too, the pair
@@ -46,20 +47,26 @@ namespace g2 {
 constexpr int BM = 128;           // rows of A per CTA (256 per pair)
 constexpr int BN = 128;           // columns of B per CTA (256 per pair)
 constexpr int BK = 64;            // k per stage: 128 bytes of bf16, one swizzle row
-constexpr int STAGES = 6;            // 192 KB of ring (7 measured no faster)
 constexpr int A_BYTES = BM * BK * 2;   // 16 KB
 constexpr int B_BYTES = BN * BK * 2;   // 16 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+// ring depth: 6 stages (192 KB; 7 measured no faster), 5 in the v-hat form
+template <bool VHAT>
+struct Cfg {
+    static constexpr int ST = VHAT ? 5 : 6;
+    static constexpr int RING = ST * STAGE_BYTES;
+    static constexpr int BAR_OFF = RING;                 // barriers + TMEM slot: 256 B
+    static constexpr int VH_OFF = RING + 256;            // v-hat transposition tiles + column sums
+    static constexpr int VH_BYTES = VHAT ? (4 * 32 * 33 + 2 * 4 * 256) * 4 : 0;
+    static constexpr int STG_OFF = VH_OFF + VH_BYTES;    // output staging: 4 warps x 2 x (32 x 32 bf16)
+    static constexpr int STG_BYTES = 4 * 2 * 2048;
+    static constexpr size_t SMEM = (size_t)STG_OFF + STG_BYTES + 1024 /* alignment slack */;
+};
+constexpr int VH_TR_FLOATS = 4 * 32 * 33;
 constexpr int THREADS = 192;      // warp 0 TMA, warp 1 MMA / TMEM, warps 2-5 epilogue
 constexpr int ACC_COLS = 256;     // fp32 columns of one accumulator
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint64_t WAIT_NS = 2000000000ull;   // 2 s of GPU time per wait
-constexpr size_t SMEM_BYTES = (size_t)STAGES * STAGE_BYTES + 1024 /* align */ + 256 /* barriers */;
-// v-hat epilogue: per-warp 32 x 33 transposition tiles and two buffers of the
-// four warps' column partials of a tile
-constexpr int VH_TR_FLOATS = 4 * 32 * 33;
-constexpr int VH_CP_FLOATS = 2 * 4 * 256;
-constexpr size_t SMEM_BYTES_VHAT = SMEM_BYTES + (size_t)(VH_TR_FLOATS + VH_CP_FLOATS) * 4;
 
 struct Params {
     int M, N, K;
@@ -229,14 +236,17 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 template <bool VHAT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm2sm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                   const __grid_constant__ Params P) {
+                   const __grid_constant__ CUtensorMap map_d, const __grid_constant__ Params P) {
+    using C = Cfg<VHAT>;
+    constexpr int STAGES = C::ST;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
     // full[STAGES], empty[STAGES], tmem_full[2], tmem_empty[2], then the TMEM base slot
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
-    float* vh_tr = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES + 256);   // VHAT only
+    float* vh_tr = reinterpret_cast<float*>(smem + C::VH_OFF);   // VHAT only
     float* vh_cp = vh_tr + VH_TR_FLOATS;
+    uint8_t* stg = smem + C::STG_OFF;
     const uint32_t bar0 = smem_u32(bars);
     auto full = [&](int s) { return bar0 + 8u * s; };
     auto empty = [&](int s) { return bar0 + 8u * (STAGES + s); };
@@ -326,7 +336,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             if (!mbar_wait(tfull(acc), aph, P.err, 4)) goto done;
             tc_fence_after();
             const int row = tm * 2 * BM + (int)rank * BM + q * 32 + lane;
-            __nv_bfloat16* drow = P.D + (long long)row * P.ldd;
             float rsum = 0.0f;
 #pragma unroll 1
             for (int c = 0; c < ACC_COLS; c += 32) {
@@ -343,19 +352,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                       "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
                     : "r"(ta));
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                const int col = tn * 2 * BN + c;
-                if (row < P.M) {
+                // the warp's 32 rows x 32 columns as bf16 through a shared staging
+                // buffer (two per warp, alternating) and one TMA tile store, which
+                // clips what lies beyond M and N
+                {
+                    uint8_t* sb = stg + (q * 2 + ((c >> 5) & 1)) * 2048;
+                    if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+                    __syncwarp();
+                    uint4* dst = reinterpret_cast<uint4*>(sb + lane * 64);
 #pragma unroll
                     for (int v = 0; v < 4; ++v) {
-                        const int cc = col + v * 8;
-                        if (cc < P.N) {      // N is a multiple of 8: a chunk is all in or all out
-                            uint4 o;
-                            o.x = pack_bf16(__uint_as_float(r[v * 8 + 0]), __uint_as_float(r[v * 8 + 1]));
-                            o.y = pack_bf16(__uint_as_float(r[v * 8 + 2]), __uint_as_float(r[v * 8 + 3]));
-                            o.z = pack_bf16(__uint_as_float(r[v * 8 + 4]), __uint_as_float(r[v * 8 + 5]));
-                            o.w = pack_bf16(__uint_as_float(r[v * 8 + 6]), __uint_as_float(r[v * 8 + 7]));
-                            *reinterpret_cast<uint4*>(drow + cc) = o;
-                        }
+                        uint4 o;
+                        o.x = pack_bf16(__uint_as_float(r[v * 8 + 0]), __uint_as_float(r[v * 8 + 1]));
+                        o.y = pack_bf16(__uint_as_float(r[v * 8 + 2]), __uint_as_float(r[v * 8 + 3]));
+                        o.z = pack_bf16(__uint_as_float(r[v * 8 + 4]), __uint_as_float(r[v * 8 + 5]));
+                        o.w = pack_bf16(__uint_as_float(r[v * 8 + 6]), __uint_as_float(r[v * 8 + 7]));
+                        dst[v] = o;
+                    }
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) {
+                        asm volatile(
+                            "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                                reinterpret_cast<uint64_t>(&map_d)),
+                            "r"(smem_u32(sb)), "r"(tn * 2 * BN + c), "r"(row - lane)
+                            : "memory");
+                        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
                     }
                 }
                 if constexpr (VHAT) {
@@ -402,6 +424,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         }
     }
 done:
+    if (warp >= 2 && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");   // output stores landed
     tc_fence_before();
     __syncthreads();
     cluster_sync();     // no barrier or tensor memory of the pair is used after this
@@ -431,7 +454,7 @@ EncodeTiledFn encode_fn() {
 // tensor map over a row-major bf16 matrix [rows, cols] (row stride ld
 // elements), box {box_inner (cols), box_outer (rows)}, 128-byte swizzle
 bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_inner,
-              int box_outer) {
+              int box_outer, bool swizzle = true) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return false;
     cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
@@ -439,7 +462,8 @@ bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int6
     cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer};
     cuuint32_t estr[2] = {1, 1};
     return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -463,9 +487,9 @@ int resident_pairs() {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(2 * (sms / 2), 1, 1);
         cfg.blockDim = dim3(THREADS, 1, 1);
-        cfg.dynamicSmemBytes = SMEM_BYTES;
+        cfg.dynamicSmemBytes = Cfg<false>::SMEM;
         int n = 0;
-        cudaFuncSetAttribute(gemm2sm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
+        cudaFuncSetAttribute(gemm2sm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg<false>::SMEM);
         if (cudaOccupancyMaxActiveClusters(&n, gemm2sm_kernel<false>, &cfg) != cudaSuccess || n <= 0) {
             cudaGetLastError();
             n = sms / 2;
@@ -493,18 +517,13 @@ int gemm2sm(const void* A, int a_mn, int64_t lda, const void* B, int b_mn, int64
     if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B) | reinterpret_cast<uintptr_t>(D)) % 16)
         return fail(CONCORD_EALIGN, std::string(name) + ": operands must be 16-byte aligned");
     if (int rc = bind_current_context(name)) return rc;
-    CUtensorMap ma, mb;
+    CUtensorMap ma, mb, md;
     const bool ok_a = a_mn ? make_map(&ma, A, K, M, lda, 64, 64) : make_map(&ma, A, M, K, lda, 64, 128);
     const bool ok_b = b_mn ? make_map(&mb, B, K, N, ldb, 64, 64) : make_map(&mb, B, N, K, ldb, 64, 128);
-    if (!ok_a || !ok_b) return fail(CONCORD_ELAUNCH, std::string(name) + ": TMA descriptor encoding failed");
+    const bool ok_d = make_map(&md, D, M, N, ldd, 32, 32, false);     // output: 32 x 32 tile stores
+    if (!ok_a || !ok_b || !ok_d) return fail(CONCORD_ELAUNCH, std::string(name) + ": TMA descriptor encoding failed");
     int* err = error_word();
     if (!err) return fail(CONCORD_ELAUNCH, std::string(name) + ": no error word");
-    static int sms = [] {
-        int d = 0, n = 148;
-        cudaGetDevice(&d);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d);
-        return n > 1 ? n : 148;
-    }();
     Params P{};
     P.M = (int)M; P.N = (int)N; P.K = (int)K;
     P.tiles_m = (int)((M + 255) / 256);
@@ -521,19 +540,16 @@ int gemm2sm(const void* A, int a_mn, int64_t lda, const void* B, int b_mn, int64
     P.err = err;
     P.rp = rp; P.cp = cp; P.ldrp = ldrp; P.ldcp = ldcp;
     const int tiles = P.tiles_m * P.tiles_n;
-    // as many pairs as can be resident at once (a cluster needs two free SMs
-    // of one GPC, so this can be below half the SM count)
-    const int max_pairs = resident_pairs();
-    const int pairs = std::min(tiles, max_pairs);
+    const int pairs = std::min(tiles, resident_pairs());
     static bool attr = [] {
         return cudaFuncSetAttribute(gemm2sm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)SMEM_BYTES) == cudaSuccess &&
+                                    (int)Cfg<false>::SMEM) == cudaSuccess &&
                cudaFuncSetAttribute(gemm2sm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)SMEM_BYTES_VHAT) == cudaSuccess;
+                                    (int)Cfg<true>::SMEM) == cudaSuccess;
     }();
     if (!attr) return fail(CONCORD_ELAUNCH, std::string(name) + ": shared-memory attribute refused");
-    if (rp && cp) gemm2sm_kernel<true><<<2 * pairs, THREADS, SMEM_BYTES_VHAT, stream>>>(ma, mb, P);
-    else gemm2sm_kernel<false><<<2 * pairs, THREADS, SMEM_BYTES, stream>>>(ma, mb, P);
+    if (rp && cp) gemm2sm_kernel<true><<<2 * pairs, THREADS, Cfg<true>::SMEM, stream>>>(ma, mb, md, P);
+    else gemm2sm_kernel<false><<<2 * pairs, THREADS, Cfg<false>::SMEM, stream>>>(ma, mb, md, P);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(CONCORD_ELAUNCH, std::string(name) + ": " + cudaGetErrorString(e));
     return CONCORD_OK;
