@@ -25,9 +25,12 @@ def _ok(*dims):
 
 
 def _workspace(M, N, K, device):
+    """GEMM scratch (CUTLASS workspace, split-K partials) per (device, current
+    stream), grown on demand: launches on one stream are ordered, and a buffer
+    replaced on one stream was never used by another."""
     lib = _abi.load()
     need = lib.concord_gemm_workspace_bytes(M, N, K)
-    key = str(device)
+    key = (str(device), torch.cuda.current_stream(device).cuda_stream)
     buf = _WS.get(key)
     if buf is None or buf.numel() < max(need, 1):
         buf = torch.empty(max(need, 256), dtype=torch.uint8, device=device)
