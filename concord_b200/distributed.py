@@ -291,6 +291,9 @@ class RowShardedStep:
         # optional dict name -> CUDA event, recorded after each phase of the peer
         # transport's step (instrumentation for the bench's phase breakdown)
         self.phase_events = None
+        # column maxima all-reduced once per step for many layers
+        # (DeferredColumnMaxima) instead of after this layer's step
+        self.deferred = None
         self.peer = None
         if transport == "peer":
             wbuf, _, _ = layer._ensure_buffers()
@@ -326,6 +329,8 @@ class RowShardedStep:
 
     @torch.no_grad()
     def step(self, grad_local):
+        if self.deferred is not None:
+            self.deferred.pending = True
         L, kern, g = self.layer, self.kernels, self.group
         N, K, S, r0, r1 = self.N, self.K, self.S, self.r0, self.r1
         n_loc = r1 - r0
@@ -360,9 +365,10 @@ class RowShardedStep:
             # same ordering protects the receive buffers: a rank pushes its next
             # dW only after the v-hat all-reduce, i.e. after every rank finished
             # reading this one.
-            self.peer.allreduce(cmax if track else None, _abi.PEER_MAX_I32)
-            if "allreduce_cmax" in ph:
-                ph["allreduce_cmax"].record()
+            if self.deferred is None:
+                self.peer.allreduce(cmax if track else None, _abi.PEER_MAX_I32)
+                if "allreduce_cmax" in ph:
+                    ph["allreduce_cmax"].record()
             return
         # 1. reduce-scatter of the bf16 gradient over rows
         if self.even and grad_local.is_contiguous():
@@ -386,7 +392,7 @@ class RowShardedStep:
         wdst = wbuf[r0:r1] if self.even else self.wshard[:n_loc]
         self._step_shard(params_of(L), n_loc, wdst, rmax, cmax)
         # 4. column maxima and the forward weight to every rank
-        if track:
+        if track and self.deferred is None:
             dist.all_reduce(cmax, op=dist.ReduceOp.MAX, group=g)
         if self.even:
             _all_gather(wbuf, wbuf[r0:r1], g)                 # in place
@@ -411,6 +417,8 @@ class RowShardedStep:
     @torch.no_grad()
     def rebalance(self, fired_out=None):
         """The layer's rebalance() on this rank's rows, with the shared column maxima."""
+        if self.deferred is not None:
+            self.deferred.sync()      # a no-op unless a step ran since the last sync
         L = self.layer
         if L.allow_tickdown:
             raise NotImplementedError("tick-down needs whole-matrix column medians; "
@@ -443,3 +451,61 @@ class RowShardedStep:
                 full = torch.zeros((self.P * S,) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
                 _all_gather(full, loc, g)
                 t.copy_(full[:N])
+
+
+class DeferredColumnMaxima:
+    """One all-reduce of the column maxima of many row-sharded layers per step.
+
+    Each RowShardedStep ends its step with a cross-rank rendezvous: the
+    all-reduce (max) of the layer's column maxima, which rebalance() needs,
+    and which, on the peer transport, is also what guarantees that every
+    rank's forward-weight rows have landed before the next forward reads them.
+    A model of hundreds of layers pays that rendezvous (tens of microseconds
+    of waiting for the slowest rank at 8 GPUs) once per layer.  This object
+    takes the steppers of one model: their layers' column-maxima buffers
+    become views of one flat int32 buffer, their steps skip the per-layer
+    all-reduce, and `sync()` all-reduces the flat buffer once (NCCL, max).
+
+    `sync()` must run after the backward and before the next forward: the
+    first `rebalance()` of any of these layers calls it, so a training loop
+    that rebalances (or calls `sync()`) after every backward needs no other
+    change.  Every rank must call it equally often (it is a collective).
+    Results are identical to the per-layer all-reduce.
+    """
+
+    def __init__(self, steppers, group=None):
+        steppers = list(steppers)
+        if not steppers:
+            raise ValueError("no steppers")
+        dev = steppers[0].layer.packed_w.device
+        self.group = group
+        self.steppers = steppers
+        self.flat = torch.zeros(sum(st.K for st in steppers), dtype=torch.int32, device=dev)
+        off = 0
+        for st in steppers:
+            if st.deferred is not None:
+                raise RuntimeError("a stepper can belong to one DeferredColumnMaxima only")
+            L = st.layer
+            L._ensure_buffers()
+            view = self.flat[off:off + st.K]
+            view.copy_(L._col_max_buf)
+            L._col_max_buf = view
+            st.deferred = self
+            off += st.K
+        self.pending = False
+
+    @torch.no_grad()
+    def sync(self):
+        """All-reduce (max) every layer's column maxima; a no-op when no step ran
+        since the last call."""
+        if not self.pending:
+            return
+        dist.all_reduce(self.flat, op=dist.ReduceOp.MAX, group=self.group)
+        self.pending = False
+
+    def close(self):
+        """Back to per-layer all-reduces (the layers keep their current maxima)."""
+        for st in self.steppers:
+            st.layer._col_max_buf = st.layer._col_max_buf.clone()
+            st.deferred = None
+

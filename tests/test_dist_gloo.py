@@ -98,7 +98,7 @@ def make_layer(seed=0):
     bufs = (torch.zeros(N, K, dtype=torch.bfloat16), torch.zeros(N, dtype=torch.int32),
             torch.zeros(K, dtype=torch.int32))
     L._bf16_weight_buf, L._row_max_buf, L._col_max_buf = bufs
-    L._ensure_buffers = lambda: bufs
+    L._ensure_buffers = lambda: (L._bf16_weight_buf, L._row_max_buf, L._col_max_buf)
     return L
 
 
@@ -113,12 +113,24 @@ def _worker(rank, world, port, out_dir, mode="manual"):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
-    from concord_b200.distributed import RowShardedStep
+    from concord_b200.distributed import DeferredColumnMaxima, RowShardedStep
     L = make_layer()
     st = RowShardedStep(L, kernels=OracleKernels())
     from concord_b200 import packed_b as pb
+    dm = other = None
+    if mode == "deferred":
+        # a second layer first in the flat buffer, so this layer's maxima sit at an offset
+        other = RowShardedStep(make_layer(seed=1), kernels=OracleKernels())
+        dm = DeferredColumnMaxima([other, st])
     for s in range(3):
-        if mode == "manual":
+        if mode == "deferred":
+            other.step(grads(s + 10, rank))
+            st.step(grads(s, rank))
+            assert dm.pending
+            st.rebalance()              # all-reduces both layers' maxima once
+            assert not dm.pending
+            other.rebalance()
+        elif mode == "manual":
             st.step(grads(s, rank))
             st.rebalance()
         else:
@@ -127,7 +139,10 @@ def _worker(rank, world, port, out_dir, mode="manual"):
             pb._optimizer_half(SimpleNamespace(packed_w=L.packed_w), grads(s, rank))
             pb.ConcordLinearPackedB.rebalance(L)
     st.gather_state()
-    if mode != "manual":
+    if dm is not None:
+        dm.close()
+        other.close()
+    if mode == "backward":
         assert pb._sharded_of(L.packed_w) is st
         st.close()
         assert pb._sharded_of(L.packed_w) is None
@@ -192,11 +207,13 @@ def _free_port():
 import pytest  # noqa: E402
 
 
-@pytest.mark.parametrize("mode", ["manual", "backward"])
+@pytest.mark.parametrize("mode", ["manual", "backward", "deferred"])
 def test_row_sharded_step_two_ranks(tmp_path, oracle_mod, mode):
     """`manual`: the caller hands each rank's dW to RowShardedStep.step.
     `backward`: the layer's own backward path (registered as data-parallel)
-    hands it over; both must give the same sharded state."""
+    hands it over.  `deferred`: the column maxima of two layers are
+    all-reduced once per step (DeferredColumnMaxima) instead of per layer.
+    All must give the same sharded state."""
     world = 2
     mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path), mode), nprocs=world,
                        join=True, start_method="spawn")

@@ -12,6 +12,7 @@ checkpoint is read.
   vocab 32000, seq 2048) on uniform random token ids.
 """
 import math
+import os
 import time
 
 import torch
@@ -249,6 +250,17 @@ def run_steps(step_fn, refill, steps, warmup, layers, lr, graph, world=1, group=
     return times, losses
 
 
+def _defer_column_maxima(steppers, group):
+    """On more than one rank: every layer's column maxima all-reduced once per
+    step (the first rebalance() of the step does it) instead of once per
+    layer inside the backward.  CONCORD_DP_DEFER_CMAX=0 keeps the per-layer
+    all-reduce."""
+    if not steppers or os.environ.get("CONCORD_DP_DEFER_CMAX", "1") == "0":
+        return None
+    from concord_b200.distributed import DeferredColumnMaxima
+    return DeferredColumnMaxima(steppers, group=group)
+
+
 def allreduce_grads(params, flat, world, group=None):
     """Average the ordinary parameters' gradients over the ranks (one bucket)."""
     import torch.distributed as dist
@@ -354,6 +366,7 @@ def train_llama_dp(steps, warmup, batch_per_gpu=8, seq=2048, lr=5e-4, aux_lr=0.0
     if world > 1:
         from concord_b200.distributed import RowShardedStep
         steppers = [RowShardedStep(l, group=group) for l in layers]
+    deferred = _defer_column_maxima(steppers, group)
     aux = [p for p in model.parameters() if p.requires_grad]
     opt = torch.optim.SGD(aux, lr=aux_lr, momentum=0.9)
     flat = torch.zeros(sum(p.numel() for p in aux), dtype=torch.float32, device=dev)
@@ -381,6 +394,8 @@ def train_llama_dp(steps, warmup, batch_per_gpu=8, seq=2048, lr=5e-4, aux_lr=0.0
     for st in steppers:
         st.check()
     params = sum(l.packed_w.numel() for l in layers)
+    if deferred is not None:
+        deferred.close()
     for st in steppers:
         st.close()
     return dict(ms=times, losses=losses, concord_params=params, world=world,
@@ -579,6 +594,7 @@ def train_sdxl_dp(steps, warmup, batch_per_gpu=4, res=128, lr=5e-5, aux_lr=1e-4,
     if world > 1:
         from concord_b200.distributed import RowShardedStep
         steppers = [RowShardedStep(l, group=group) for l in layers]
+    deferred = _defer_column_maxima(steppers, group)
     aux = [p for p in model.parameters() if p.requires_grad]
     opt = torch.optim.SGD(aux, lr=aux_lr, momentum=0.9)
     flat = torch.zeros(sum(p.numel() for p in aux), dtype=torch.float32, device=dev)
@@ -620,6 +636,8 @@ def train_sdxl_dp(steps, warmup, batch_per_gpu=4, res=128, lr=5e-5, aux_lr=1e-4,
     out = dict(ms=times, losses=losses, params=n_total, concord_params=sum(l.packed_w.numel() for l in layers),
                n_layers=len(layers), world=world, samples_per_step=world * batch_per_gpu,
                state_gb=base_mem / 1e9, peak_gb=torch.cuda.max_memory_allocated() / 1e9)
+    if deferred is not None:
+        deferred.close()
     for st in steppers:
         st.close()
     return out
