@@ -356,7 +356,7 @@ extern "C" int concord_rebalance_gated(const concord_reb_layer* layers, int32_t 
 }
 
 extern "C" size_t concord_rebalance_workspace_bytes(int64_t N, int64_t K) {
-    if (N <= 0 || K <= 0) return 0;
+    if (N < 0 || K <= 0) return 0;
     return 256 + al256((size_t)N) + al256((size_t)K) + al256((size_t)N * HB * 4) + al256((size_t)K * HB * 4) +
            al256((size_t)N * 4) + al256((size_t)K * 4);
 }
@@ -370,7 +370,10 @@ extern "C" int concord_rebalance(int32_t* packed, int64_t ldp, int8_t* row_exp, 
                                  void* stream) {
     if (!packed || !row_exp || !col_exp || !row_max || !col_max || !seed)
         return fail(CONCORD_EINVAL, "concord_rebalance: null pointer");
-    if (N <= 0 || K <= 0 || ldp < K || row0 < 0 || N_total < row0 + N)
+    // N == 0 (a data-parallel rank that owns no rows of the layer): the
+    // column decisions still tick the shared column exponents, fold the column
+    // high-watermarks and bump the seed; there is no word to shift
+    if (N < 0 || K <= 0 || ldp < K || row0 < 0 || N_total < row0 + N || N_total <= 0)
         return fail(CONCORD_ESHAPE, "concord_rebalance: bad shape/stride");
     if (allow_tickdown && N_total != N)
         return fail(CONCORD_EINVAL, "concord_rebalance: tick-down needs the whole matrix (column medians)");
@@ -396,6 +399,7 @@ extern "C" int concord_rebalance(int32_t* packed, int64_t ldp, int8_t* row_exp, 
     if (cudaMemsetAsync(A.fired, 0, 3 * sizeof(int32_t), s) != cudaSuccess) return check_launch("concord_rebalance");
     int64_t blocks = (N * K + RB_THREADS - 1) / RB_THREADS;
     if (blocks > 148 * 32) blocks = 148 * 32;
+    if (blocks < 1) blocks = 1;
     // the histogram bins sit at shape-dependent offsets of a workspace that
     // callers may share between layers of different shapes: clear them first
     if (allow_tickdown &&

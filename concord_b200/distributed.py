@@ -425,9 +425,8 @@ class RowShardedStep:
                                       "not supported on a row-sharded layer")
         rmax, cmax = L._row_max_buf, L._col_max_buf
         r0, r1 = self.r0, self.r1
-        if r1 <= r0:
-            L._reb_seed.add_(1)
-            return
+        # a rank that owns no rows still applies the shared column decisions
+        # (column exponents, column high-watermarks, the seed): zero rows
         self.kernels.rebalance(L.packed_w[r0:r1], L.row_exp[r0:r1], L.col_exp, rmax[r0:r1], cmax,
                                L._row_max_hwm[r0:r1], L._col_max_hwm, L._reb_seed, L.MAX_M,
                                L.EXP_MAX, L.EXP_MIN, r0, self.N, fired_out)

@@ -402,7 +402,7 @@ void oracle_vhat_ex(const uint16_t* grad, int64_t ldg, int64_t N, int64_t K,
         v_row[n] = b2 * v_row[n] + omb2 * t;
     }
     for (int64_t k = 0; k < K; ++k) {
-        float t = cp[k];
+        float t = nrb > 0 ? cp[k] : 0.0f;   /* a shard of no rows contributes zero */
         for (int64_t b = 1; b < nrb; ++b) t = t + cp[b * K + k];
         if (col_sum_out) col_sum_out[k] = t;
         else v_col[k] = b2 * v_col[k] + omb2 * t;

@@ -72,39 +72,39 @@ class OracleKernels:
         return self._salt
 
 
-def make_layer_W(seed=0):
+def make_layer_W(seed=0, n=N):
     rng = np.random.default_rng(seed)
-    return (rng.standard_normal((N, K)) * 0.05).astype(np.float32)
+    return (rng.standard_normal((n, K)) * 0.05).astype(np.float32)
 
 
-def make_layer(seed=0):
+def make_layer(seed=0, n=N):
     from oracle import oracle
     from concord_b200.packed_b import compute_drift_cancel_C
     rng = np.random.default_rng(seed)
-    W = (rng.standard_normal((N, K)) * 0.05).astype(np.float32)
+    W = (rng.standard_normal((n, K)) * 0.05).astype(np.float32)
     packed, rexp, cexp = oracle.quantize(W)
     L = SimpleNamespace(
         packed_w=torch.from_numpy(packed), row_exp=torch.from_numpy(rexp),
-        col_exp=torch.from_numpy(cexp), v_row=torch.zeros(N), v_col=torch.zeros(K),
-        _sum_v_inv=torch.ones(1), _coh_pre=torch.ones(N, K), _lr_buf=torch.tensor([0.5]),
+        col_exp=torch.from_numpy(cexp), v_row=torch.zeros(n), v_col=torch.zeros(K),
+        _sum_v_inv=torch.ones(1), _coh_pre=torch.ones(n, K), _lr_buf=torch.tensor([0.5]),
         _eps_buf=torch.tensor([1e-10]), track_rebalance=True, adafactor_beta2=0.999,
         optimizer_kind='adamw', alpha=0.1, beta1=0.0, weight_decay=0.0, step_cap=10.0,
         v_scale=0.0, precond_p=0.5, gf_consol=0.0,
         drift_cancel_C=compute_drift_cancel_C(0.1, 0.001), alpha_v_fast=0.001, wd_sv=0.0,
         wd_sf=0.0, mass_preserve_v=True, apply_chase=True, gf_trust_delta_sq=1.0,
         MANTISSA_BIAS=15, MAX_M=24000, EXP_MAX=7, EXP_MIN=-8, allow_tickdown=False,
-        _reb_seed=torch.zeros(1, dtype=torch.int32), _row_max_hwm=torch.zeros(N, dtype=torch.int32),
+        _reb_seed=torch.zeros(1, dtype=torch.int32), _row_max_hwm=torch.zeros(n, dtype=torch.int32),
         _col_max_hwm=torch.zeros(K, dtype=torch.int32))
-    bufs = (torch.zeros(N, K, dtype=torch.bfloat16), torch.zeros(N, dtype=torch.int32),
+    bufs = (torch.zeros(n, K, dtype=torch.bfloat16), torch.zeros(n, dtype=torch.int32),
             torch.zeros(K, dtype=torch.int32))
     L._bf16_weight_buf, L._row_max_buf, L._col_max_buf = bufs
     L._ensure_buffers = lambda: (L._bf16_weight_buf, L._row_max_buf, L._col_max_buf)
     return L
 
 
-def grads(step, rank):
+def grads(step, rank, n=N):
     g = torch.Generator().manual_seed(100 * step + rank)
-    return (torch.randn(N, K, generator=g) * 1e-3).to(torch.bfloat16)
+    return (torch.randn(n, K, generator=g) * 1e-3).to(torch.bfloat16)
 
 
 def _worker(rank, world, port, out_dir, mode="manual"):
@@ -114,7 +114,8 @@ def _worker(rank, world, port, out_dir, mode="manual"):
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     from concord_b200.distributed import DeferredColumnMaxima, RowShardedStep
-    L = make_layer()
+    n = 1 if mode == "empty_rank" else N     # rank 1 of 2 owns no row of a 1-row layer
+    L = make_layer(n=n)
     st = RowShardedStep(L, kernels=OracleKernels())
     from concord_b200 import packed_b as pb
     dm = other = None
@@ -130,8 +131,8 @@ def _worker(rank, world, port, out_dir, mode="manual"):
             st.rebalance()              # all-reduces both layers' maxima once
             assert not dm.pending
             other.rebalance()
-        elif mode == "manual":
-            st.step(grads(s, rank))
+        elif mode in ("manual", "empty_rank"):
+            st.step(grads(s, rank, n))
             st.rebalance()
         else:
             # what the layer's autograd backward and rebalance() do once the
@@ -155,12 +156,12 @@ def _worker(rank, world, port, out_dir, mode="manual"):
     dist.destroy_process_group()
 
 
-def emulate(world):
+def emulate(world, n=N):
     """Single-process emulation of the sharded arithmetic (same order as 2 ranks)."""
     from oracle import oracle
     from concord_b200.packed_b import adamw_params
-    L = make_layer()
-    S = (N + world - 1) // world
+    L = make_layer(n=n)
+    S = (n + world - 1) // world
     coh = L._coh_pre.numpy()
     packed, v_row, v_col = L.packed_w.numpy(), L.v_row.numpy(), L.v_col.numpy()
     svi = np.ones(1, np.float32)
@@ -168,24 +169,24 @@ def emulate(world):
                      mass_preserve=True, gf_trust_delta_sq=1.0, use_cohpre=True)
     rexp, cexp = L.row_exp.numpy(), L.col_exp.numpy()
     seed = np.zeros(1, np.int32)
-    hr, hc = np.zeros(N, np.int32), np.zeros(K, np.int32)
-    wbuf = np.zeros((N, K), np.uint16)
+    hr, hc = np.zeros(n, np.int32), np.zeros(K, np.int32)
+    wbuf = np.zeros((n, K), np.uint16)
     for s in range(3):
-        tot = grads(s, 0).float()
+        tot = grads(s, 0, n).float()
         for r in range(1, world):
-            tot = tot + grads(s, r).float()
+            tot = tot + grads(s, r, n).float()
         g = _np_bf16(tot.to(torch.bfloat16))
         cs_sum, vs_sum = np.zeros(K, np.float32), np.zeros(1, np.float32)
         for r in range(world):
-            r0, r1 = r * S, min(N, r * S + S)
+            r0, r1 = r * S, min(n, r * S + S)
             cs, vs = oracle.vhat_partial(np.ascontiguousarray(g[r0:r1]), v_row[r0:r1])
             cs_sum = cs_sum + cs
             vs_sum = vs_sum + vs
         v_col[:] = np.float32(0.999) * v_col + np.float32(1.0 - 0.999) * cs_sum
         svi[0] = np.float32(1.0) / np.maximum(vs_sum[0], np.float32(1e-30))
-        rmax, cmax = np.zeros(N, np.int32), np.zeros(K, np.int32)
+        rmax, cmax = np.zeros(n, np.int32), np.zeros(K, np.int32)
         for r in range(world):
-            r0, r1 = r * S, min(N, r * S + S)
+            r0, r1 = r * S, min(n, r * S + S)
             w = np.zeros((r1 - r0, K), np.uint16)
             oracle.step(P, packed[r0:r1], np.ascontiguousarray(g[r0:r1]), w, rexp[r0:r1], cexp,
                         rmax[r0:r1], cmax, v_row[r0:r1], v_col, svi, coh[r0:r1],
@@ -207,24 +208,28 @@ def _free_port():
 import pytest  # noqa: E402
 
 
-@pytest.mark.parametrize("mode", ["manual", "backward", "deferred"])
+@pytest.mark.parametrize("mode", ["manual", "backward", "deferred", "empty_rank"])
 def test_row_sharded_step_two_ranks(tmp_path, oracle_mod, mode):
     """`manual`: the caller hands each rank's dW to RowShardedStep.step.
     `backward`: the layer's own backward path (registered as data-parallel)
     hands it over.  `deferred`: the column maxima of two layers are
     all-reduced once per step (DeferredColumnMaxima) instead of per layer.
-    All must give the same sharded state."""
+    `empty_rank`: a 1-row layer, so rank 1 owns no row; it must still apply
+    the shared column decisions of the rebalance.  All must give the same
+    sharded state."""
     world = 2
+    n = 1 if mode == "empty_rank" else N
     mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path), mode), nprocs=world,
                        join=True, start_method="spawn")
     r = [dict(np.load(tmp_path / f"rank{i}.npz")) for i in range(world)]
-    ref = emulate(world)
+    ref = emulate(world, n)
     for key in ("packed", "v_row", "v_col", "svi", "wbuf", "cmax", "coh", "row_exp", "col_exp",
                 "seed", "hwm"):
         np.testing.assert_array_equal(r[0][key], r[1][key], err_msg=key)
         np.testing.assert_array_equal(r[0][key], ref[key], err_msg=key)
     from oracle import oracle
-    assert (r[0]["row_exp"] != oracle.quantize(make_layer_W())[1]).any(), "rebalance never fired"
+    q = oracle.quantize(make_layer_W(n=n))
+    assert (r[0]["row_exp"] != q[1]).any() and (r[0]["col_exp"] != q[2]).any(), "rebalance never fired"
 
 
 def _failing_worker(rank, world, port, out_dir):
