@@ -560,7 +560,7 @@ def bench_sdxl(args, rank, world, steps=None, warmup=None, ret=False):
     emit(d)
 
 
-def model_steps(args, rank, world):
+def model_steps(args, rank, world, out=None):
     """The training steps of configs 5 and 4 on every rank, in the same run as
     the packed-step line: BASELINE's scaling half ("SDXL UNet train steps/s at
     1/2/4/8") and the data-parallel decoder, each a weak-scaling whole-job
@@ -569,10 +569,11 @@ def model_steps(args, rank, world):
     recorded in the line instead of ending the run."""
     import gc
     steps, warmup = max(3, min(args.steps, 10)), max(3, min(args.warmup, 5))
-    out = {"note": "whole-job weak-scaling throughput at this GPU count (fixed per-GPU batch); "
+    out = {} if out is None else out
+    out["note"] = ("whole-job weak-scaling throughput at this GPU count (fixed per-GPU batch); "
                    "llama: config 5, 8 sequences x 2048 tokens per GPU; sdxl: config 4, 4 latents per GPU, "
                    "coh_pre gate on; each through loss.backward() with the row-sharded packed step "
-                   f"on more than one GPU; {steps} timed steps after {warmup} eager ones"}
+                   f"on more than one GPU; {steps} timed steps after {warmup} eager ones")
     for name, fn in (("llama", bench_llama), ("sdxl", bench_sdxl)):
         try:
             line = fn(args, rank, world, steps=steps, warmup=warmup, ret=True)
@@ -586,6 +587,33 @@ def model_steps(args, rank, world):
         gc.collect()
         torch.cuda.empty_cache()
     return out
+
+
+def model_steps_guarded(args, rank, world, line):
+    """model_steps under a wall-clock limit (CONCORD_BENCH_MODEL_LIMIT seconds,
+    default 540): if the model workloads have not finished by then (a first
+    run at a new GPU count that is slow to set up, or a rank stuck in a
+    collective), rank 0 prints `line` with the results finished so far and an
+    error note, and every rank exits 0, so the packed-step line is never lost."""
+    import threading
+    limit = float(os.environ.get("CONCORD_BENCH_MODEL_LIMIT", "540"))
+    out = {}
+
+    def fire():
+        if rank == 0 and line is not None:
+            part = dict(out)
+            part["error"] = f"model workloads did not finish within {limit:.0f} s; results so far"
+            line["weak_scaling"] = part
+            emit(line)
+        sys.stdout.flush()
+        os._exit(0)
+    timer = threading.Timer(limit, fire)
+    timer.daemon = True
+    timer.start()
+    try:
+        return model_steps(args, rank, world, out)
+    finally:
+        timer.cancel()
 
 
 CONV_SHAPES = [  # B, C, O, H=W, k (SDXL UNet channel counts, stride 1)
@@ -815,13 +843,14 @@ def main():
     from concord_b200 import packed_b
     packed_b._lib()
     r = bench_ours(args, rank, world, device)
-    models = None if args.no_models else model_steps(args, rank, world)
     hbm, tf, src = peaks()
     # one layer update per step whatever the GPU count (the update is sharded)
     value = r["bytes_step"] / (r["ms"] * 1e-3) / 1e9
     shard_params = r["params"] if world == 1 else SHARDED.S * args.cols
     achieved = shard_params * STEP_BYTES_PER_PARAM / (r["step_kernel_ms"] * 1e-3) / 1e9
     if rank != 0:
+        if not args.no_models:
+            model_steps_guarded(args, rank, world, None)
         return
     d = base_line(args, world)
     flops = 2.0 * M * args.rows * args.cols
@@ -855,8 +884,6 @@ def main():
                               "per step: [peer reduce 1] + vhat partial 1 + finish 1 + step 1 + rebalance 2; "
                               "plus NCCL collectives (not counted)"),
     })
-    if models is not None:
-        d["weak_scaling"] = models
     if world == 1:
         bms, fms = backward_time(args.rows, args.cols, device)
         packed_b.set_fused_dw_vhat(False)
@@ -870,7 +897,7 @@ def main():
                                  "dW GEMM with the v-hat partials in its epilogue + v-hat fold, packed step, "
                                  "then rebalance(); CUDA events, eager.  ms_vhat_separate: the same with "
                                  "the dW GEMM and a standalone v-hat launch"}
-    if not args.no_cpu_baseline:
+    if not args.no_cpu_baseline and world == 1:     # the CPU baseline is a one-GPU figure
         v1, dt = cpu_baseline(rows=2048, threads=1)
         port = {"value": v1, "unit": "GB/s", "cores": 1, "kind": "port",
                 "sample": f"2048 rows x {args.cols} cols (v-hat + step), {dt:.2f} s; oracle port (C restatement)"}
@@ -885,6 +912,8 @@ def main():
             d["cpu_baseline_port"] = port
         else:
             d["cpu_baseline"] = port
+    if not args.no_models:
+        d["weak_scaling"] = model_steps_guarded(args, rank, world, d)
     emit(d)
     if world > 1:
         dist.destroy_process_group()
