@@ -33,6 +33,9 @@
 
 #include <stdlib.h>
 
+#include <algorithm>
+#include <atomic>
+#include <mutex>
 #include <string>
 
 #include "../../include/concord_b200.h"
@@ -479,24 +482,39 @@ int* error_word() {
 
 // CTA pairs of the 2-SM GEMM that can be resident at once (a cluster needs
 // two free SMs of one GPC, so this can be below half the SM count)
+// Per-device set-up, once per device (a process may drive several GPUs): the
+// kernels' shared-memory limit and the number of resident pairs.  Returns the
+// pair count, or 0 when the attribute was refused.
+constexpr int MAX_DEVICES = 64;
 int resident_pairs() {
-    static const int n_pairs = [] {
-        int d = 0, sms = 148;
-        cudaGetDevice(&d);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, d);
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(2 * (sms / 2), 1, 1);
-        cfg.blockDim = dim3(THREADS, 1, 1);
-        cfg.dynamicSmemBytes = Cfg<false>::SMEM;
-        int n = 0;
-        cudaFuncSetAttribute(gemm2sm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg<false>::SMEM);
-        if (cudaOccupancyMaxActiveClusters(&n, gemm2sm_kernel<false>, &cfg) != cudaSuccess || n <= 0) {
-            cudaGetLastError();
-            n = sms / 2;
-        }
-        return std::min(n, sms / 2);
-    }();
-    return n_pairs;
+    static std::atomic<int> pairs_of[MAX_DEVICES];   // 0: not set up yet
+    static std::mutex mu;
+    int d = 0;
+    if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= MAX_DEVICES) return 0;
+    int n = pairs_of[d].load();
+    if (n > 0) return n;
+    std::lock_guard<std::mutex> g(mu);
+    if ((n = pairs_of[d].load()) > 0) return n;
+    if (cudaFuncSetAttribute(gemm2sm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)Cfg<false>::SMEM) != cudaSuccess ||
+        cudaFuncSetAttribute(gemm2sm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)Cfg<true>::SMEM) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, d);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (sms / 2), 1, 1);
+    cfg.blockDim = dim3(THREADS, 1, 1);
+    cfg.dynamicSmemBytes = Cfg<false>::SMEM;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm2sm_kernel<false>, &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        n = sms / 2;
+    }
+    n = std::max(1, std::min(n, sms / 2));
+    pairs_of[d].store(n);
+    return n;
 }
 
 }  // namespace g2
@@ -540,14 +558,9 @@ int gemm2sm(const void* A, int a_mn, int64_t lda, const void* B, int b_mn, int64
     P.err = err;
     P.rp = rp; P.cp = cp; P.ldrp = ldrp; P.ldcp = ldcp;
     const int tiles = P.tiles_m * P.tiles_n;
-    const int pairs = std::min(tiles, resident_pairs());
-    static bool attr = [] {
-        return cudaFuncSetAttribute(gemm2sm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)Cfg<false>::SMEM) == cudaSuccess &&
-               cudaFuncSetAttribute(gemm2sm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)Cfg<true>::SMEM) == cudaSuccess;
-    }();
-    if (!attr) return fail(CONCORD_ELAUNCH, std::string(name) + ": shared-memory attribute refused");
+    const int resident = resident_pairs();
+    if (resident <= 0) return fail(CONCORD_ELAUNCH, std::string(name) + ": shared-memory attribute refused");
+    const int pairs = std::min(tiles, resident);
     if (rp && cp) gemm2sm_kernel<true><<<2 * pairs, THREADS, Cfg<true>::SMEM, stream>>>(ma, mb, md, P);
     else gemm2sm_kernel<false><<<2 * pairs, THREADS, Cfg<false>::SMEM, stream>>>(ma, mb, md, P);
     cudaError_t e = cudaGetLastError();
